@@ -1,0 +1,396 @@
+#!/usr/bin/env python3
+"""Benchmark of the W4A16 grouped-MoE layer on B200 (one JSON line on stdout).
+
+Workload (default, N=1): benchmark configuration 1 -- decode, M=1 token, one
+MoE layer with E=256 experts, top-10, H=3072, I=1024, int4 group-32 weights
+(random-init, seeded), bf16 activations ~ N(0,1).  A "step" is one full
+``fused_experts_w4a16`` call: routing align + w13 GEMM (+SiLU*up) + w2 GEMM
+(+ weighted top-k sum).  ``value`` is achieved weight bandwidth: unique routed
+experts x 5,308,416 bytes per step / device time per step (the reference's
+metric, bench/bench_moe.py:250-263, :742-743).  Each step is replayed from a
+CUDA graph (as the reference's --cudagraph mode) with a 256 MiB L2 flush
+before it, outside the timed events.
+
+``--impl reference`` times the reference algorithm's CPU path (the numpy
+oracle port; the reference itself is PyTorch and cannot travel to the GPU box)
+on all host cores, same config and metric.  With N>1 GPUs every rank runs its
+own replica of the workload (weak scaling); rank 0 prints the aggregate.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+PKG = REPO / "gb10-laguna-s-2.1-w4a16-moe_b200"
+for _p in (str(PKG), str(REPO)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+E, TOPK, H, I, GROUP = 256, 10, 3072, 1024, 32
+BYTES_PER_EXPERT = 2 * I * (H // 2) + H * (I // 2) + 2 * I * (H // GROUP) * 2 + H * (I // GROUP) * 2
+W13_BYTES_PER_EXPERT = 2 * I * (H // 2) + 2 * I * (H // GROUP) * 2
+FLUSH_BYTES = 256 << 20
+METRIC = "weight_GBps"
+
+
+def _peaks() -> dict:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.is_file():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "src": "fallback"}
+
+
+def _traffic(M: int) -> float | None:
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+    p = REPO / "profiles" / "traffic.json"
+    if not p.is_file():
+        return None
+    d = json.loads(p.read_text())
+    v = d.get(f"w13_M{M}")
+    return float(v) if v is not None else None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:  # noqa: BLE001
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:  # noqa: BLE001
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _dist():
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def _max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def _barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def cpu_port_time(M: int, layer_cpu: dict, hidden, tw, ids, threads: int, budget_s: float,
+                  max_iters: int) -> tuple[float, int]:
+    """Mean seconds of one oracle forward on the host cores (bounded sample)."""
+    import numpy as np
+    from threadpoolctl import threadpool_limits
+
+    from oracle import moe_oracle as O
+
+    x = hidden.float().cpu().numpy()
+    tw_c = tw.float().cpu().numpy()
+    ids_c = ids.cpu().numpy().astype(np.int64)
+    times = []
+    with threadpool_limits(limits=threads):
+        t_end = time.perf_counter() + budget_s
+        while len(times) < max_iters and (not times or time.perf_counter() < t_end):
+            t0 = time.perf_counter()
+            O.moe_reference(x, layer_cpu["w1_q"], layer_cpu["w1_s"], layer_cpu["w2_q"], layer_cpu["w2_s"],
+                            tw_c, ids_c, GROUP)
+            times.append(time.perf_counter() - t0)
+    return sum(times) / len(times), len(times)
+
+
+def routed_layer_to_cpu(layer: dict, ids):
+    """Copy only the routed experts to host memory (ids remapped to them)."""
+    import numpy as np
+    import torch
+
+    used = torch.unique(ids).to(torch.int64)
+    bits = lambda t: t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)  # noqa: E731
+    sub = {"w1_q": layer["w1_q"][used].cpu().numpy(), "w1_s": bits(layer["w1_s"][used]),
+           "w2_q": layer["w2_q"][used].cpu().numpy(), "w2_s": bits(layer["w2_s"][used])}
+    remap = torch.full((E,), -1, dtype=torch.int64, device=ids.device)
+    remap[used] = torch.arange(used.numel(), device=ids.device)
+    return sub, remap[ids.to(torch.int64)]
+
+
+def run_reference_arm(args) -> int:
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import torch
+
+    from kernels.synthetic import make_hidden, make_layer, make_routing
+
+    M = args.M
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    layer = make_layer(E, H, I, seed=0, device=dev)
+    hidden = make_hidden(M, H)
+    tw, ids = make_routing(M, E, TOPK)
+    n_act = int(torch.unique(ids).numel())
+    wbytes = n_act * BYTES_PER_EXPERT
+    sub, local_ids = routed_layer_to_cpu(layer, ids.to(dev))
+    del layer
+    cores = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        cpu_port_time(M, sub, hidden, tw, local_ids.cpu(), cores, 0.0, 1)
+    per, n = cpu_port_time(M, sub, hidden, tw, local_ids.cpu(), cores, 1e9, args.steps)
+    gbs = wbytes / per / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": world,
+        "steps": n, "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"decode M={M} (config 1): E=256 top-10 H=3072 I=1024 int4 g32",
+                   "M": M, "unique_experts": n_act, "weight_bytes_per_step": wbytes},
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"{n} full forwards of the numpy oracle (restating bench/bench_moe.py:"
+                                   f"run_reference, per-call dequant) at M={M} on the routed experts"},
+        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args) -> int:
+    import torch
+
+    from kernels import w4a16_moe as K
+    from kernels.synthetic import make_hidden, make_layer, make_routing
+
+    world, rank, local = _dist()
+    if world == 1 and args.gpus > 1:
+        print("note: --gpus > 1 requested without torchrun; running one replica", file=sys.stderr)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    K.load_library()
+    M = args.M
+
+    layer = make_layer(E, H, I, seed=0, device=dev)
+    w1r, s1r = K.repack_weights(layer["w1_q"], layer["w1_s"])
+    w2r, s2r = K.repack_weights(layer["w2_q"], layer["w2_s"])
+    hidden = make_hidden(M, H, device=dev)
+    tw, ids = make_routing(M, E, TOPK, device=dev)
+    n_act = int(torch.unique(ids).numel())
+    wbytes = n_act * BYTES_PER_EXPERT
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def step(h, w, i):
+        return K.fused_experts_w4a16(h, w1r, w2r, s1r, s2r, w, i)
+
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    K.set_stage_events(ev)
+    for _ in range(max(args.warmup, 3)):
+        step(hidden, tw, ids)
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step(hidden, tw, ids)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out_static = step(hidden, tw, ids)
+    for _ in range(max(args.warmup, 3)):
+        flush.zero_()
+        graph.replay()
+    torch.cuda.synchronize()
+
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    step_ms, align_ms, w13_ms, w2_ms = [], [], [], []
+    _barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        for _ in range(args.steps):
+            flush.zero_()
+            t0.record()
+            graph.replay()
+            t1.record()
+            t1.synchronize()
+            step_ms.append(t0.elapsed_time(t1))
+            align_ms.append(ev[0].elapsed_time(ev[1]))
+            w13_ms.append(ev[1].elapsed_time(ev[2]))
+            w2_ms.append(ev[2].elapsed_time(ev[3]))
+        torch.cuda.synchronize()
+    _barrier(world)
+    K.set_stage_events(None)
+    total_ms = _max_over_ranks(sum(step_ms), world)
+    total_bytes = _sum_over_ranks(float(wbytes * args.steps), world)
+    value = total_bytes / (total_ms * 1e-3) / 1e9
+
+    # ---- end to end through the public API with pinned host buffers ----
+    h_host = hidden.cpu().pin_memory()
+    tw_host = tw.cpu().pin_memory()
+    ids_host = ids.cpu().pin_memory()
+    out_host = torch.empty((M, H), dtype=torch.bfloat16).pin_memory()
+    hd, twd, idd = torch.empty_like(hidden), torch.empty_like(tw), torch.empty_like(ids)
+    e2e_ms = []
+    for it in range(args.warmup + args.steps):
+        flush.zero_()
+        t0.record()
+        hd.copy_(h_host, non_blocking=True)
+        twd.copy_(tw_host, non_blocking=True)
+        idd.copy_(ids_host, non_blocking=True)
+        o = step(hd, twd, idd)
+        out_host.copy_(o, non_blocking=True)
+        t1.record()
+        t1.synchronize()
+        if it >= args.warmup:
+            e2e_ms.append(t0.elapsed_time(t1))
+    e2e_total = _max_over_ranks(sum(e2e_ms), world)
+    e2e_value = total_bytes / (e2e_total * 1e-3) / 1e9
+    h2d = hidden.numel() * 2 + tw.numel() * 4 + ids.numel() * 4
+    d2h = M * H * 2
+
+    # ---- parity spot check of the timed output (cheap, outside timing) ----
+    torch.cuda.synchronize()
+    assert torch.isfinite(out_static.float()).all()
+    assert torch.equal(out_host.to(dev), out_static)
+
+    peaks = _peaks()
+    w13_mean = sum(w13_ms) / len(w13_ms)
+    w13_bytes = n_act * W13_BYTES_PER_EXPERT
+    achieved = w13_bytes / (w13_mean * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "traffic": _traffic(M),
+                "kernel": "moe_gemv_kernel<0,*> (w13 + SiLU*up)",
+                "peak_src": f"{peaks['src']} hbm_gbs (STREAM copy)",
+                "algorithmic_bytes_per_launch": w13_bytes}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sub, local_ids = routed_layer_to_cpu(layer, ids)
+        per, n = cpu_port_time(M, sub, hidden.cpu(), tw.cpu(), local_ids.cpu(), 1, args.cpu_budget, 1000)
+        cpu = {"value": wbytes / per / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+               "sample": f"{n} forwards (~{args.cpu_budget:.0f}s budget) of the numpy oracle (restating "
+                         f"bench/bench_moe.py:run_reference with per-call dequant) at M={M}, 1 thread"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"decode M={M} (config 1): E=256 top-10 H=3072 I=1024 int4 g32, one layer",
+                       "M": M, "unique_experts": n_act, "weight_bytes_per_step": wbytes,
+                       "us_per_layer": 1e3 * total_ms / args.steps,
+                       "stage_us": {"align": 1e3 * sum(align_ms) / len(align_ms), "w13": 1e3 * w13_mean,
+                                    "w2": 1e3 * sum(w2_ms) / len(w2_ms)},
+                       "parallelism": f"replicas x{world}" if world > 1 else "single",
+                       "l2": "flushed before every step (256 MiB write, untimed)",
+                       "timing": "CUDA-graph replay per step, CUDA events, sum over steps, max over ranks"},
+            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "us_per_step": 1e3 * e2e_total / args.steps},
+            "gpu_launches": 3 * args.steps,
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--M", type=int, default=1, help="tokens per step (config 1: 1)")
+    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline sampling")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,116 @@
+"""Build recipe for the sm_100a shared library ``lib/libw4a16moe_b200.so``.
+
+Compiles every ``csrc/*.cu`` with nvcc for ``sm_100a`` only and links one
+position-independent shared object that exports the C ABI declared in
+``include/w4a16_moe_b200.h``.  Incremental: a source newer than the library
+(or a changed flag set) triggers a rebuild.
+
+Usage: ``python build.py [--force] [--jobs N]``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import hashlib
+import os
+import shutil
+import subprocess
+import sys
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+PKG_DIR = Path(__file__).resolve().parent
+REPO_DIR = PKG_DIR.parent
+CSRC = PKG_DIR / "csrc"
+INCLUDE = REPO_DIR / "include"
+BUILD_DIR = PKG_DIR / "_build"
+LIB_DIR = PKG_DIR / "lib"
+LIB_NAME = "libw4a16moe_b200.so"
+
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = [
+    "-O3",
+    "-std=c++17",
+    "-lineinfo",
+    "-Xcompiler",
+    "-fPIC",
+    "-Xcompiler",
+    "-fvisibility=hidden",
+    "--expt-relaxed-constexpr",
+    "-DW4A16_BUILD",
+]
+
+
+def nvcc_path() -> str:
+    cand = shutil.which("nvcc")
+    if cand:
+        return cand
+    for p in ("/usr/local/cuda/bin/nvcc",):
+        if os.path.exists(p):
+            return p
+    raise RuntimeError("nvcc not found: the sm_100a library cannot be built")
+
+
+def _flags_digest(extra: list[str]) -> str:
+    return hashlib.sha1(" ".join(ARCH_FLAGS + NVCC_FLAGS + extra).encode()).hexdigest()[:12]
+
+
+def lib_path() -> Path:
+    return LIB_DIR / LIB_NAME
+
+
+def _needs_build(sources: list[Path], headers: list[Path], out: Path, stamp: Path, digest: str) -> bool:
+    if not out.exists() or not stamp.exists() or stamp.read_text().strip() != digest:
+        return True
+    t = out.stat().st_mtime
+    return any(p.stat().st_mtime > t for p in sources + headers)
+
+
+def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -> Path:
+    nvcc = nvcc_path()
+    sources = sorted(CSRC.glob("*.cu"))
+    headers = sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
+    out = lib_path()
+    stamp = BUILD_DIR / "flags.sha1"
+    digest = _flags_digest([])
+    if not force and not _needs_build(sources, headers, out, stamp, digest):
+        return out
+    BUILD_DIR.mkdir(parents=True, exist_ok=True)
+    LIB_DIR.mkdir(parents=True, exist_ok=True)
+
+    def compile_one(src: Path) -> Path:
+        obj = BUILD_DIR / (src.stem + ".o")
+        cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, f"-I{INCLUDE}", "-c", str(src), "-o", str(obj)]
+        if verbose:
+            cmd.insert(1, "-Xptxas=-v")
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"nvcc failed for {src.name}:\n{res.stdout}\n{res.stderr}")
+        if verbose and res.stderr:
+            print(res.stderr, file=sys.stderr)
+        return obj
+
+    with ThreadPoolExecutor(max_workers=jobs or min(8, os.cpu_count() or 1)) as ex:
+        objs = list(ex.map(compile_one, sources))
+    tmp = out.with_suffix(".so.tmp")
+    cmd = [nvcc, *ARCH_FLAGS, "-shared", "-o", str(tmp), *map(str, objs), "-lcudart"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
+    os.replace(tmp, out)
+    stamp.write_text(digest)
+    return out
+
+
+def main(argv: list[str] | None = None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("--jobs", type=int, default=None)
+    ap.add_argument("--verbose", action="store_true", help="print ptxas register/spill info")
+    args = ap.parse_args(argv)
+    print(build(force=args.force, jobs=args.jobs, verbose=args.verbose))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,148 @@
+// Shared definitions for the B200 W4A16 grouped-MoE library.
+//
+// Repacked weight layout ("fragment-major"), produced by repack.cu and read by
+// every GEMM kernel in this library:
+//
+//   w_rep  (E, N_out/16, K/64, 512)  uint8
+//   s_rep  (E, N_out/16, K/64, 32)   bf16
+//
+// One (expert, row-tile of 16 output rows, k-chunk of 64) block of weights is
+// 512 contiguous bytes = 32 lanes x 16 bytes.  Lane l (g = l>>2, t = l&3) owns
+// four 32-bit words, one per 16-wide k step j (k0 = chunk*64 + j*16).  Word j
+// holds eight 4-bit codes (stored value q+8 in [0,15]) at nibble positions:
+//
+//   n0 = W[g  ][k0+2t  ]   n4 = W[g  ][k0+2t+1]
+//   n1 = W[g+8][k0+2t  ]   n5 = W[g+8][k0+2t+1]
+//   n2 = W[g  ][k0+2t+8]   n6 = W[g  ][k0+2t+9]
+//   n3 = W[g+8][k0+2t+8]   n7 = W[g+8][k0+2t+9]
+//
+// so that (w >> 4i) & 0x000F000F yields, for i = 0..3, exactly the bf16 pairs
+// a warp-level m16n8k16 A fragment wants (a0a1, a2a3, a4a5, a6a7).  The same
+// block is decoded by the tensor-core prefill kernel into its smem tiles.
+//
+// Scales: per (expert, row-tile, chunk) 32 bf16; quad g holds
+//   [4g+0] = s(g, grp0)  [4g+1] = s(g+8, grp0)  [4g+2] = s(g, grp1)  [4g+3] = s(g+8, grp1)
+// where grp0/grp1 are the two 32-wide groups of the chunk.  Group sizes that
+// are multiples of 32 are stored by replicating each scale (exact).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace w4moe {
+
+constexpr int kRowTile = 16;
+constexpr int kChunkK = 64;
+constexpr int kChunkBytes = 512;   // packed weight bytes per (rowtile, chunk)
+constexpr int kChunkScales = 32;   // bf16 scales per (rowtile, chunk)
+constexpr int kGroup = 32;         // storage group size
+
+// Status codes returned by every C-ABI entry point.
+enum Status : int {
+  kOk = 0,
+  kInvalidArgument = 1,
+  kUnsupported = 2,
+  kCudaError = 3,
+};
+
+// (a & b) | c in one LOP3.
+__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// Decode one fragment word into four bf16x2 registers holding (q-8)*s,
+// rounded once to bf16 (the same value a dequantise-then-bf16 reference
+// produces).  The nibble is OR-ed into the mantissa of 128.0 (0x4300), which
+// makes the bf16 value 128+code exactly; subtracting 136 leaves code-8.
+// sg / sg8: the bf16 scale for rows g and g+8, broadcast to both halves.
+__device__ __forceinline__ void dequant_word(uint32_t w, uint32_t sg, uint32_t sg8,
+                                             uint32_t (&a)[4]) {
+  const uint32_t kMask = 0x000F000Fu;
+  const uint32_t kMagic = 0x43004300u;   // bf16 {128, 128}
+  const uint32_t kBias = 0x43084308u;    // bf16 {136, 136}
+  a[0] = bf16x2_mul(bf16x2_sub(and_or(w, kMask, kMagic), kBias), sg);
+  a[1] = bf16x2_mul(bf16x2_sub(and_or(w >> 4, kMask, kMagic), kBias), sg8);
+  a[2] = bf16x2_mul(bf16x2_sub(and_or(w >> 8, kMask, kMagic), kBias), sg);
+  a[3] = bf16x2_mul(bf16x2_sub(and_or(w >> 12, kMask, kMagic), kBias), sg8);
+}
+
+__device__ __forceinline__ uint32_t bcast_bf16(uint16_t s) {
+  return (uint32_t)s | ((uint32_t)s << 16);
+}
+
+// D = A(16x16 bf16, row) * B(16x8 bf16, col) + D, fp32 accumulate.
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4],
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ uint2 ldg_stream2(const uint2* p) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+               : "=r"(r.x), "=r"(r.y)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + __expf(-v)); }
+
+// Maps a flat slot (m*topk + t) to the local expert it is routed to, or -1.
+// ids are int32 or int64; expert_map (nullable) is the vLLM expert-parallel
+// table from global expert id to local id (-1 = not on this rank).
+struct SlotMap {
+  const void* ids;
+  int ids_is_64;
+  const int32_t* expert_map;
+  int global_E;
+  int E;  // local experts
+
+  __device__ __forceinline__ int operator()(int slot) const {
+    long long v = ids_is_64 ? (long long)((const int64_t*)ids)[slot]
+                            : (long long)((const int32_t*)ids)[slot];
+    if (expert_map != nullptr) {
+      if (v < 0 || v >= global_E) return -1;
+      v = expert_map[v];
+    }
+    return (v >= 0 && v < E) ? (int)v : -1;
+  }
+};
+
+// Routing arrays derived once per forward by the align kernel and consumed by
+// the GEMM kernels.  All live in the caller-provided workspace.
+struct RouteView {
+  const int32_t* sorted;      // [P] slot ids grouped by expert, padded per expert
+  const int32_t* offsets;     // [E+1] padded start of each expert in `sorted`
+  const int32_t* counts;      // [E] valid slots per expert
+  const int32_t* active;      // [E] compact list of experts with count > 0
+  const int32_t* num_active;  // [1]
+  const int32_t* tok_valid;   // [M] locally routed slots per token
+};
+
+}  // namespace w4moe

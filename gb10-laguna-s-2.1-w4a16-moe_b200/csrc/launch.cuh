@@ -1,0 +1,66 @@
+// Parameter blocks and host launchers of every kernel in this library.
+#pragma once
+
+#include "common.cuh"
+
+namespace w4moe {
+
+// ---- align.cu ----
+struct AlignParams {
+  SlotMap map;              // ids (+ optional expert_map) -> local expert
+  int n_tok;
+  int topk;
+  int E;                    // (local) experts
+  int bs;
+  int P;
+  int32_t* sorted;          // [P]
+  int32_t* expert_ids;      // [P/bs]
+  int32_t* num_post;        // [1]
+  // optional outputs (nullable)
+  int32_t* counts;          // [E]
+  int32_t* offsets;         // [E+1]
+  int32_t* active;          // [E]
+  int32_t* num_active;      // [1]
+  int32_t* tok_valid;       // [n_tok/topk]
+  __nv_bfloat16* zero_rows; // [M, H] rows zeroed where tok_valid == 0
+  int H;
+};
+cudaError_t launch_align(const AlignParams& p, cudaStream_t stream);
+
+// ---- repack.cu ----
+struct RepackParams {
+  const uint8_t* w_q;       // (E, N_out, K/2)
+  const uint16_t* scales;   // (E, N_out, K/G) bf16 bits
+  int E, N_out, K, G;
+  uint32_t* w_rep;          // (E, N_out/16, K/64, 128) words
+  uint16_t* s_rep;          // (E, N_out/16, K/64, 32)
+};
+cudaError_t launch_repack(const RepackParams& p, cudaStream_t stream);
+
+// ---- gemv.cu ----
+struct GemvParams {
+  const uint4* w;            // fragment-major weights of this projection
+  const uint2* s;            // scale quads
+  int n_rowtiles;            // N_out / 16
+  int n_chunks;              // K / 64
+  const __nv_bfloat16* x;    // B operand rows
+  long long x_ld;            // row stride in elements
+  int x_row_div;             // row of slot = slot / x_row_div
+  RouteView rt;
+  int topk;
+  int items_per_expert;
+  // MODE 0 epilogue
+  __nv_bfloat16* inter;
+  int I;
+  // MODE 1 epilogue
+  float* partial;
+  int H;
+  const float* topk_w;       // [n_tok]
+  int32_t* counters;         // [M * items_per_expert], zero between calls
+  __nv_bfloat16* out;        // [M, H]
+  SlotMap map;
+};
+cudaError_t launch_gemv(const GemvParams& p, int mode, int ng, int grid, cudaStream_t stream);
+int gemv_blocks_per_sm(int mode, int ng);
+
+}  // namespace w4moe

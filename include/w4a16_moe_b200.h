@@ -1,0 +1,110 @@
+/*
+ * C ABI of the B200 (sm_100a) W4A16 grouped-MoE library.
+ *
+ * Every entry point takes raw device pointers, 64-bit sizes and a CUDA stream
+ * passed as `void*` (a cudaStream_t; NULL = legacy default stream), launches
+ * asynchronously on that stream and returns a status:
+ *   0 = ok, 1 = invalid argument, 2 = unsupported shape, 3 = CUDA error.
+ * On a nonzero status w4a16_last_error() returns a message for the calling
+ * thread.  No entry point allocates device memory, synchronises the device or
+ * copies between host and device, so all of them can be captured in a CUDA
+ * graph once the workspace exists.
+ *
+ * Tensors (all row-major, contiguous unless a leading dimension is given):
+ *   bf16 values are passed as their 16-bit patterns.
+ *   Packed int4 weights use the vLLM / compressed-tensors post-load layout:
+ *   (E, N_out, K/2) uint8, byte j of a row = element 2j (low nibble) and
+ *   2j+1 (high nibble), stored value = q + 8, q in [-8, 7].
+ */
+#ifndef W4A16_MOE_B200_H_
+#define W4A16_MOE_B200_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define W4A16_API __attribute__((visibility("default")))
+#else
+#define W4A16_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Message for the last failing call on this thread ("" if none). */
+W4A16_API const char* w4a16_last_error(void);
+
+/* Library ABI version (major*100 + minor). */
+W4A16_API int w4a16_version(void);
+
+/*
+ * Profiling hook (no reference counterpart): for the calling thread, have
+ * w4a16_moe_forward record events[i] (cudaEvent_t handles) on its stream at
+ * stage boundaries: 0 before routing, 1 after routing, 2 after the w13 GEMM,
+ * 3 after the w2 GEMM.  Works inside CUDA-graph capture (external event
+ * records).  n_events = 0 disables it.
+ */
+W4A16_API int w4a16_set_stage_events(void* const* events, int n_events);
+
+/*
+ * Length P of sorted_token_ids for moe_align_block_size:
+ * roundup(n_tok + num_experts*(block_size-1), block_size).
+ * Replaces the sizing in kernels/w4a16_moe.py:153-157 (_align_workspace).
+ */
+W4A16_API int64_t w4a16_align_buffer_len(int64_t n_tok, int64_t num_experts, int64_t block_size);
+
+/*
+ * Expert-sorted, block-padded slot order.  Bit-exact with the reference's
+ * moe_align_block_size (kernels/w4a16_moe.py:187-290):
+ *   sorted_token_ids [P]            int32, padding = M*topk
+ *   expert_ids       [P/block_size] int32, -1 past num_tokens_post_padded
+ *   num_tokens_post_padded [1]      int32
+ * topk_ids: [M, topk] int32 (ids_is_int64 = 0) or int64 (1).
+ * num_experts <= 1024.
+ */
+W4A16_API int w4a16_moe_align(const void* topk_ids, int ids_is_int64, int64_t M, int64_t topk,
+                    int64_t num_experts, int64_t block_size, int32_t* sorted_token_ids,
+                    int32_t* expert_ids, int32_t* num_tokens_post_padded, void* stream);
+
+/*
+ * Load-time weight transform into this library's fragment-major layout.
+ * Replaces repack_weights (kernels/w4a16_moe.py:63-116).
+ *   w_q     (E, N_out, K/2) uint8        scales (E, N_out, K/group_size) bf16
+ *   w_rep   (E, N_out/16, K/64, 512) u8  s_rep  (E, N_out/16, K/64, 32) bf16
+ * Requires N_out % 16 == 0, K % 64 == 0, group_size % 32 == 0, K % group_size == 0.
+ */
+W4A16_API int w4a16_repack(const uint8_t* w_q, const void* scales, int64_t E, int64_t N_out, int64_t K,
+                 int64_t group_size, uint8_t* w_rep, void* s_rep, void* stream);
+
+/* Bytes of workspace w4a16_moe_forward needs for this shape. */
+W4A16_API int64_t w4a16_moe_workspace_size(int64_t M, int64_t topk, int64_t E, int64_t H, int64_t I);
+
+/*
+ * Fused W4A16 MoE layer: routing align -> w13 GEMM + SiLU(gate)*up -> w2 GEMM
+ * with the router-weighted top-k sum fused in.
+ * Replaces fused_experts_w4a16 (kernels/w4a16_moe.py:678-909).
+ *
+ *   hidden        [M, H] bf16, row stride hidden_ld elements
+ *   w13_rep/s13   repacked (E, 2I/16, H/64, ...) gate rows [0,I), up rows [I,2I)
+ *   w2_rep/s2     repacked (E, H/16, I/64, ...)
+ *   topk_weights  [M, topk] fp32          topk_ids [M, topk] int32 / int64
+ *   expert_map    nullable [global_num_experts] int32: global id -> local id
+ *                 in [0, E) or -1 (slot skipped), the vLLM EP convention
+ *   out           [M, H] bf16 (fully written; rows with no local slot are 0)
+ *   workspace     >= w4a16_moe_workspace_size bytes, 256-byte aligned, ZERO-
+ *                 FILLED BEFORE ITS FIRST USE; every call leaves it reusable.
+ *                 Calls sharing one workspace must be stream-ordered.
+ * Requires H % 64 == 0, I % 64 == 0, E <= 1024.
+ */
+W4A16_API int w4a16_moe_forward(const void* hidden, int64_t M, int64_t H, int64_t hidden_ld,
+                      const void* w13_rep, const void* s13_rep, const void* w2_rep,
+                      const void* s2_rep, int64_t E, int64_t I, const float* topk_weights,
+                      const void* topk_ids, int ids_is_int64, int64_t topk,
+                      const int32_t* expert_map, int64_t global_num_experts, void* out,
+                      void* workspace, int64_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* W4A16_MOE_B200_H_ */

@@ -1,0 +1,293 @@
+"""GPU parity of the sm_100a library (through its C ABI) against the CPU oracle
+and the reference-generated golden fixtures.
+
+Bars: routing outputs bit-exact; MoE output within
+relative Frobenius error 1e-2 of the fp32 reference everywhere, and max-abs
+2e-2 at configuration 0.  At the 3072-wide layer |out| reaches ~28, where bf16
+output rounding alone exceeds 2e-2, so there the max-abs bar is taken relative
+to max|ref| (<= 1e-2) and reported.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+REL_FROB_TOL = 1e-2
+MAX_ABS_TOL_CFG0 = 2e-2
+MAX_ABS_REL_TOL = 1e-2
+
+
+@pytest.fixture(scope="module")
+def K():
+    import build as build_mod
+
+    build_mod.build()
+    from kernels import w4a16_moe
+
+    return w4a16_moe
+
+
+def _bits(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def oracle_for(hidden, layer, tw, ids, tokens=None, expert_map=None):
+    """fp32 oracle on the experts the selected tokens use (weights copied from
+    the device, so both sides read identical bytes)."""
+    x = hidden.float().cpu().numpy()
+    ids_c = ids.cpu().numpy().astype(np.int64)
+    tw_c = tw.float().cpu().numpy()
+    if tokens is not None:
+        x, ids_c, tw_c = x[tokens], ids_c[tokens], tw_c[tokens]
+    if expert_map is not None:
+        emap = expert_map.cpu().numpy().astype(np.int64)
+        ids_c = np.where(emap[ids_c] >= 0, emap[ids_c], -1)
+    used = np.unique(ids_c[ids_c >= 0])
+    sel = torch.as_tensor(used, device=layer["w1_q"].device)
+    w1 = layer["w1_q"][sel].cpu().numpy()
+    s1 = _bits(layer["w1_s"][sel])
+    w2 = layer["w2_q"][sel].cpu().numpy()
+    s2 = _bits(layer["w2_s"][sel])
+    local = np.where(ids_c >= 0, np.searchsorted(used, np.maximum(ids_c, 0)), -1)
+    return O.moe_reference(x, w1, s1, w2, s2, tw_c, local, 32)
+
+
+def check_close(out, ref, max_abs_tol=None, what=""):
+    o = out.float().cpu().numpy()
+    rf = O.rel_frobenius(o, ref)
+    ma = O.max_abs_err(o, ref)
+    scale = float(np.max(np.abs(ref))) + 1e-12
+    print(f"[{what}] rel_frob={rf:.3e} max_abs={ma:.3e} max_abs/max|ref|={ma / scale:.3e} max|ref|={scale:.2f}")
+    assert np.isfinite(o).all()
+    assert rf <= REL_FROB_TOL, (what, rf)
+    if max_abs_tol is not None:
+        assert ma <= max_abs_tol, (what, ma)
+    else:
+        assert ma / scale <= MAX_ABS_REL_TOL, (what, ma, scale)
+    return rf, ma
+
+
+# ---------------------------------------------------------------------------
+# routing
+# ---------------------------------------------------------------------------
+
+
+def test_align_bitexact_vs_reference_fixtures(K, golden_dir):
+    d = np.load(golden_dir / "align_cases.npz")
+    names = sorted({k.split("__")[0] for k in d.files})
+    for name in names:
+        M, topk, E, bs = (int(v) for v in d[f"{name}__meta"])
+        ids = torch.as_tensor(d[f"{name}__ids"]).cuda()
+        s, e, n = K.moe_align_block_size(ids, bs, E)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(s.cpu().numpy(), d[f"{name}__sorted"], err_msg=name)
+        np.testing.assert_array_equal(e.cpu().numpy(), d[f"{name}__expert_ids"], err_msg=name)
+        np.testing.assert_array_equal(n.cpu().numpy(), d[f"{name}__num_post"], err_msg=name)
+
+
+@pytest.mark.parametrize("M,topk,E,bs", [(1, 10, 256, 16), (256, 10, 256, 16), (4096, 10, 256, 128),
+                                         (16384, 10, 256, 128), (8192, 8, 1024, 64), (333, 1, 3, 1)])
+def test_align_bitexact_vs_oracle(K, M, topk, E, bs):
+    g = torch.Generator().manual_seed(M + E)
+    ids = torch.topk(torch.randn(M, E, generator=g), k=topk, dim=-1).indices.to(torch.int32)
+    s, e, n = K.moe_align_block_size(ids.cuda(), bs, E)
+    rs, re_, rn = O.align_block_size(ids.numpy(), bs, E)
+    np.testing.assert_array_equal(s.cpu().numpy(), rs)
+    np.testing.assert_array_equal(e.cpu().numpy(), re_)
+    np.testing.assert_array_equal(n.cpu().numpy(), rn)
+
+
+# ---------------------------------------------------------------------------
+# repack
+# ---------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("E,N,Kdim,group", [(3, 32, 128, 32), (2, 256, 512, 64), (1, 48, 256, 128)])
+def test_repack_bitexact(K, E, N, Kdim, group):
+    g = torch.Generator().manual_seed(E * N + group)
+    w = torch.randint(0, 256, (E, N, Kdim // 2), generator=g, dtype=torch.uint8)
+    s = (torch.rand(E, N, Kdim // group, generator=g) * 0.015 + 0.005).to(torch.bfloat16)
+    wr, sr = K.repack_weights(w.cuda(), s.cuda())
+    ow, os_ = O.repack_layout(w.numpy(), _bits(s), group)
+    np.testing.assert_array_equal(wr.cpu().numpy(), ow)
+    np.testing.assert_array_equal(_bits(sr), os_)
+
+
+# ---------------------------------------------------------------------------
+# forward: configuration 0 against the reference-generated golden output
+# ---------------------------------------------------------------------------
+
+
+def _cfg0_from_golden(golden_dir):
+    c = np.load(golden_dir / "config0.npz")
+    t = lambda a: torch.as_tensor(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    hidden = t(c["hidden_bits"].view(np.int16)).view(torch.bfloat16)
+    layer = {
+        "w1_q": t(c["w1_q"]), "w1_s": t(c["w1_s_bits"].view(np.int16)).view(torch.bfloat16),
+        "w2_q": t(c["w2_q"]), "w2_s": t(c["w2_s_bits"].view(np.int16)).view(torch.bfloat16),
+    }
+    return c, hidden, layer, t(c["topk_weights"]), t(c["topk_ids"])
+
+
+def test_forward_config0_golden(K, golden_dir):
+    c, hidden, layer, tw, ids = _cfg0_from_golden(golden_dir)
+    w1r, s1r = K.repack_weights(layer["w1_q"], layer["w1_s"])
+    w2r, s2r = K.repack_weights(layer["w2_q"], layer["w2_s"])
+    out = K.fused_experts_w4a16(hidden, w1r, w2r, s1r, s2r, tw, ids, group_size=32)
+    torch.cuda.synchronize()
+    assert out.shape == (4, 256) and out.dtype == torch.bfloat16
+    check_close(out, c["ref_out_fp32"], MAX_ABS_TOL_CFG0, "cfg0 vs reference run_reference")
+    # un-repacked (vLLM 3-D) weights go through the same path
+    out3 = K.fused_experts_w4a16(hidden, layer["w1_q"], layer["w2_q"], layer["w1_s"], layer["w2_s"], tw, ids)
+    assert torch.equal(out3, out)
+
+
+# ---------------------------------------------------------------------------
+# forward: the 256-expert / top-10 / 3072 x 1024 layer
+# ---------------------------------------------------------------------------
+
+
+@pytest.fixture(scope="module")
+def big_layer(K):
+    from kernels.synthetic import LAYER_E, LAYER_H, LAYER_I, make_layer
+
+    layer = make_layer(LAYER_E, LAYER_H, LAYER_I, seed=0, device="cuda")
+    w1r, s1r = K.repack_weights(layer["w1_q"], layer["w1_s"])
+    w2r, s2r = K.repack_weights(layer["w2_q"], layer["w2_s"])
+    layer.update(w1r=w1r, s1r=s1r, w2r=w2r, s2r=s2r)
+    return layer
+
+
+def _run(K, layer, hidden, tw, ids, **kw):
+    return K.fused_experts_w4a16(hidden, layer["w1r"], layer["w2r"], layer["s1r"], layer["s2r"], tw, ids, **kw)
+
+
+@pytest.mark.parametrize("M", [1, 4, 16, 64, 256])
+def test_forward_decode_configs(K, big_layer, M):
+    from kernels.synthetic import make_hidden, make_routing
+
+    hidden = make_hidden(M, 3072, device="cuda")
+    tw, ids = make_routing(M, 256, 10, device="cuda")
+    out = _run(K, big_layer, hidden, tw, ids)
+    torch.cuda.synchronize()
+    ref = oracle_for(hidden, big_layer, tw, ids)
+    check_close(out, ref, None, f"M={M}")
+
+
+@pytest.mark.parametrize("M", [1024, 4096, 16384])
+def test_forward_prefill_token_subset(K, big_layer, M):
+    from kernels.synthetic import make_hidden, make_routing
+
+    hidden = make_hidden(M, 3072, device="cuda")
+    tw, ids = make_routing(M, 256, 10, device="cuda")
+    out = _run(K, big_layer, hidden, tw, ids)
+    torch.cuda.synchronize()
+    toks = np.random.default_rng(M).choice(M, size=24, replace=False)
+    ref = oracle_for(hidden, big_layer, tw, ids, tokens=toks)
+    check_close(out[torch.as_tensor(toks, device="cuda")], ref, None, f"M={M} (24 tokens)")
+
+
+def test_deterministic_and_token_permutation(K, big_layer):
+    from kernels.synthetic import make_hidden, make_routing
+
+    M = 300
+    hidden = make_hidden(M, 3072, device="cuda")
+    tw, ids = make_routing(M, 256, 10, device="cuda")
+    a = _run(K, big_layer, hidden, tw, ids)
+    b = _run(K, big_layer, hidden, tw, ids)
+    assert torch.equal(a, b)
+    perm = torch.randperm(M, generator=torch.Generator().manual_seed(5)).cuda()
+    c = _run(K, big_layer, hidden[perm].contiguous(), tw[perm].contiguous(), ids[perm].contiguous())
+    assert torch.equal(c, a[perm])
+
+
+def test_linearity_in_router_weights(K, big_layer):
+    from kernels.synthetic import make_hidden, make_routing
+
+    M = 64
+    hidden = make_hidden(M, 3072, device="cuda")
+    tw, ids = make_routing(M, 256, 10, device="cuda")
+    a = _run(K, big_layer, hidden, tw, ids).float()
+    b = _run(K, big_layer, hidden, tw * 0.5, ids).float()  # power-of-two scale: exact in fp32
+    assert torch.equal(b, (a * 0.5).to(torch.bfloat16).float())
+
+
+def test_expert_map_shards_sum_to_full(K, big_layer):
+    from kernels.synthetic import make_hidden, make_routing
+
+    M = 48
+    hidden = make_hidden(M, 3072, device="cuda")
+    tw, ids = make_routing(M, 256, 10, device="cuda")
+    full = oracle_for(hidden, big_layer, tw, ids)
+    acc = np.zeros_like(full)
+    G = 4
+    for r in range(G):
+        emap = torch.full((256,), -1, dtype=torch.int32)
+        emap[r * 64:(r + 1) * 64] = torch.arange(64, dtype=torch.int32)
+        emap = emap.cuda()
+        sl = slice(r * 64, (r + 1) * 64)
+        loc = {k: big_layer[k][sl] for k in ("w1r", "s1r", "w2r", "s2r")}
+        out = K.fused_experts_w4a16(hidden, loc["w1r"], loc["w2r"], loc["s1r"], loc["s2r"], tw, ids,
+                                    expert_map=emap, global_num_experts=256)
+        torch.cuda.synchronize()
+        sub = {"w1_q": big_layer["w1_q"][sl], "w1_s": big_layer["w1_s"][sl],
+               "w2_q": big_layer["w2_q"][sl], "w2_s": big_layer["w2_s"][sl]}
+        ref = oracle_for(hidden, sub, tw, ids, expert_map=emap)
+        check_close(out, ref, None, f"shard {r}")
+        acc += out.float().cpu().numpy()
+    assert O.rel_frobenius(acc, full) <= REL_FROB_TOL
+
+
+def test_edge_cases(K, big_layer):
+    from kernels.synthetic import make_hidden, make_routing
+
+    # M == 0
+    h0 = torch.empty(0, 3072, dtype=torch.bfloat16, device="cuda")
+    e0 = torch.empty(0, 10, dtype=torch.int32, device="cuda")
+    assert _run(K, big_layer, h0, e0.float(), e0).shape == (0, 3072)
+    # int64 ids, strided hidden rows, duplicate experts inside one token, topk = 1
+    M = 9
+    base = make_hidden(M, 3072 + 64, device="cuda")
+    hidden = base[:, :3072]
+    tw, ids = make_routing(M, 256, 10, device="cuda")
+    ids[0, 1] = ids[0, 0]
+    ids[3, :] = 7
+    out = _run(K, big_layer, hidden, tw, ids.to(torch.int64))
+    ref = oracle_for(hidden, big_layer, tw, ids)
+    check_close(out, ref, None, "int64+strided+dups")
+    tw1, ids1 = make_routing(M, 256, 1, device="cuda")
+    out1 = _run(K, big_layer, hidden.contiguous(), tw1, ids1)
+    check_close(out1, oracle_for(hidden, big_layer, tw1, ids1), None, "topk=1")
+
+
+def test_cuda_graph_capture_and_replay(K, big_layer):
+    from kernels.synthetic import make_hidden, make_routing
+
+    M = 16
+    hidden = make_hidden(M, 3072, device="cuda")
+    tw, ids = make_routing(M, 256, 10, device="cuda")
+    static_h, static_tw, static_ids = hidden.clone(), tw.clone(), ids.clone()
+    _run(K, big_layer, static_h, static_tw, static_ids)  # warm (creates workspace)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        _run(K, big_layer, static_h, static_tw, static_ids)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        static_out = _run(K, big_layer, static_h, static_tw, static_ids)
+    h2 = make_hidden(M + 1, 3072, device="cuda")[:M]
+    tw2, ids2 = make_routing(M + 1, 256, 10, device="cuda")
+    static_h.copy_(h2)
+    static_tw.copy_(tw2[:M])
+    static_ids.copy_(ids2[:M])
+    graph.replay()
+    torch.cuda.synchronize()
+    eager = _run(K, big_layer, h2.contiguous(), tw2[:M].contiguous(), ids2[:M].contiguous())
+    assert torch.equal(static_out, eager)
