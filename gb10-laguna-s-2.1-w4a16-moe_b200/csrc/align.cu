@@ -74,12 +74,15 @@ __global__ void __launch_bounds__(kAlignThreads, 1) moe_align_kernel(AlignParams
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int E = p.E;
 
-  for (int i = tid; i < kAlignWarps * E; i += kAlignThreads) hist[i] = 0;
+  // Each of the first nseg warps owns one contiguous segment of the flat slot
+  // array (few segments for small inputs keep the per-expert scan short).
+  const int nseg = max(1, min(kAlignWarps, (p.n_tok + 127) / 128));
+  for (int i = tid; i < nseg * E; i += kAlignThreads) hist[i] = 0;
   __syncthreads();
 
-  // Each warp owns one contiguous segment of the flat slot array.
-  const int seg = (p.n_tok + kAlignWarps - 1) / kAlignWarps;
-  const int beg = min(p.n_tok, warp * seg), end = min(p.n_tok, beg + seg);
+  const int seg = (p.n_tok + nseg - 1) / nseg;
+  const int beg = warp < nseg ? min(p.n_tok, warp * seg) : p.n_tok;
+  const int end = warp < nseg ? min(p.n_tok, beg + seg) : p.n_tok;
   for (int i = beg + lane; i < end; i += 32) {
     int e = load_expert(p, i);
     if (e >= 0) atomicAdd(&hist[warp * E + e], 1);
@@ -101,7 +104,7 @@ __global__ void __launch_bounds__(kAlignThreads, 1) moe_align_kernel(AlignParams
     const int e = e0 + tid;
     int cnt = 0;
     if (e < E) {
-      for (int w = 0; w < kAlignWarps; ++w) {  // per-warp exclusive prefix
+      for (int w = 0; w < nseg; ++w) {  // per-segment exclusive prefix
         int h = hist[w * E + e];
         hist[w * E + e] = cnt;
         cnt += h;
@@ -128,7 +131,7 @@ __global__ void __launch_bounds__(kAlignThreads, 1) moe_align_kernel(AlignParams
     if (p.num_active) p.num_active[0] = carry_act;
   }
   __syncthreads();
-  for (int i = tid; i < kAlignWarps * E; i += kAlignThreads) hist[i] += s_off[i % E];
+  for (int i = tid; i < nseg * E; i += kAlignThreads) hist[i] += s_off[i % E];
   __syncthreads();
 
   // Order-preserving scatter: each warp walks its segment 32 slots at a time;
@@ -179,16 +182,17 @@ size_t align_smem_bytes(int E) { return (size_t)(kAlignWarps * E + 2 * E + 1) * 
 
 cudaError_t launch_align(const AlignParams& p, cudaStream_t stream) {
   const size_t smem = align_smem_bytes(p.E);
-  static thread_local int configured_for = -1;
+  // Per-device opt-in above the 48 KB default (largest size configured so far).
+  static thread_local size_t configured[64] = {0};
   if (smem > 48 * 1024) {
     int dev = 0;
     cudaGetDevice(&dev);
-    if (configured_for != dev) {
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (configured[dev] < smem) {
       cudaError_t err = cudaFuncSetAttribute(moe_align_kernel,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             227 * 1024);
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (err != cudaSuccess) return err;
-      configured_for = dev;
+      configured[dev] = smem;
     }
   }
   moe_align_kernel<<<1, kAlignThreads, smem, stream>>>(p);

@@ -31,6 +31,19 @@ int cuda_fail(cudaError_t err, const char* where) {
   return fail(kCudaError, "%s: %s", where, cudaGetErrorString(err));
 }
 
+int max_smem_optin() {
+  static thread_local int cached_dev = -1, cached = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (dev != cached_dev) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) v = 0;
+    cached_dev = dev;
+    cached = v;
+  }
+  return cached;
+}
+
 int sm_count() {
   static thread_local int cached_dev = -1, cached_sms = 0;
   int dev = 0;
@@ -47,6 +60,8 @@ int sm_count() {
 // Optional stage events (profiling hook): event i is recorded on the forward's
 // stream before align (0), after align (1), after w13 (2) and after w2 (3).
 thread_local cudaEvent_t g_stage_events[8];
+// Testing hook: route every forward through the general (multi-kernel) path.
+thread_local int g_force_general = 0;
 thread_local int g_n_stage_events = 0;
 
 void mark_stage(int i, cudaStream_t st) {
@@ -66,7 +81,7 @@ constexpr int64_t kMaxAlignBlock = 128;
 
 struct Workspace {
   int32_t *counts, *offsets, *active, *num_active, *num_post, *tok_valid;
-  int32_t *sorted, *expert_ids, *counters;
+  int32_t *sorted, *expert_ids, *counters, *ready, *sched;
   __nv_bfloat16* inter;
   float* partial;
   int64_t bytes;
@@ -85,6 +100,8 @@ Workspace carve(char* base, int64_t M, int64_t topk, int64_t E, int64_t H, int64
   const int64_t P = align_up(n_tok + E * (kMaxAlignBlock - 1), kMaxAlignBlock);
   // Zero-initialised, self-cleaning state first.
   w.counters = (int32_t*)take(4 * M * (H / 32));
+  w.ready = (int32_t*)take(4 * E);
+  w.sched = (int32_t*)take(4 * 4);
   w.counts = (int32_t*)take(4 * E);
   w.offsets = (int32_t*)take(4 * (E + 1));
   w.active = (int32_t*)take(4 * E);
@@ -109,6 +126,27 @@ extern "C" {
 const char* w4a16_last_error(void) { return g_last_error.c_str(); }
 
 int w4a16_version(void) { return 100; }
+
+int w4a16_set_path(int path) {
+  g_last_error.clear();
+  if (path < 0 || path > 1) return fail(kInvalidArgument, "w4a16_set_path: 0 = auto, 1 = general");
+  g_force_general = path;
+  return kOk;
+}
+
+int w4a16_moe_read_status(const void* workspace, int64_t M, int64_t topk, int64_t E, int64_t H, int64_t I,
+                          int32_t* status_out, void* stream) {
+  g_last_error.clear();
+  if (!workspace || !status_out) return fail(kInvalidArgument, "w4a16_moe_read_status: null pointer");
+  Workspace ws = carve((char*)workspace, M, topk, E, H, I);
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t err = cudaMemcpyAsync(status_out, ws.sched + 2, sizeof(int32_t), cudaMemcpyDeviceToHost, st);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(st);
+  if (err == cudaSuccess) err = cudaMemsetAsync(ws.sched + 2, 0, sizeof(int32_t), st);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(st);
+  if (err != cudaSuccess) return cuda_fail(err, "w4a16_moe_read_status");
+  return kOk;
+}
 
 int w4a16_set_stage_events(void* const* events, int n_events) {
   g_last_error.clear();
@@ -215,6 +253,41 @@ int w4a16_moe_forward(const void* hidden, int64_t M, int64_t H, int64_t hidden_l
   const int64_t n_tok = M * topk;
   const SlotMap map{topk_ids, ids_is_int64 ? 1 : 0, expert_map,
                     (int)(expert_map ? global_num_experts : E), (int)E};
+
+  // Small M: one fused persistent kernel (routing + w13 + w2 + top-k sum).
+  if (!g_force_general && ((uintptr_t)hidden & 15) == 0 && (hidden_ld & 7) == 0) {
+    DecodeParams dp{};
+    dp.w13 = (const uint8_t*)w13_rep;
+    dp.s13 = (const uint8_t*)s13_rep;
+    dp.w2 = (const uint8_t*)w2_rep;
+    dp.s2 = (const uint8_t*)s2_rep;
+    dp.hidden = (const __nv_bfloat16*)hidden;
+    dp.hidden_ld = hidden_ld;
+    dp.map = map;
+    dp.n_tok = (int)n_tok;
+    dp.topk = (int)topk;
+    dp.M = (int)M;
+    dp.E = (int)E;
+    dp.H = (int)H;
+    dp.I = (int)I;
+    dp.topk_w = topk_weights;
+    dp.inter = ws.inter;
+    dp.partial = ws.partial;
+    dp.out = (__nv_bfloat16*)out;
+    dp.counters = ws.counters;
+    dp.ready = ws.ready;
+    dp.sched = ws.sched;
+    dp.zero_rows = expert_map != nullptr;
+    if (decode_plan(dp, sm_count(), max_smem_optin() - 1024)) {
+      mark_stage(0, st);
+      mark_stage(1, st);
+      cudaError_t err = launch_decode(dp, st);
+      if (err != cudaSuccess) return cuda_fail(err, "w4a16_moe_forward/decode");
+      mark_stage(2, st);
+      mark_stage(3, st);
+      return kOk;
+    }
+  }
 
   // 1) routing: per-expert counts / offsets / active list (block size 1: the
   //    small-M GEMMs read each expert's exact slot range).

@@ -63,4 +63,30 @@ struct GemvParams {
 cudaError_t launch_gemv(const GemvParams& p, int mode, int ng, int grid, cudaStream_t stream);
 int gemv_blocks_per_sm(int mode, int ng);
 
+// ---- decode.cu (fused persistent small-M layer) ----
+constexpr int kDecodeMaxSlots = 4096;  // M*topk handled by the fused kernel
+
+struct DecodeParams {
+  const uint8_t* w13;        // fragment-major w13 (gate rows [0,I), up rows [I,2I))
+  const uint8_t* s13;
+  const uint8_t* w2;         // fragment-major w2
+  const uint8_t* s2;
+  const __nv_bfloat16* hidden;
+  long long hidden_ld;
+  SlotMap map;
+  int n_tok, topk, M, E, H, I;
+  const float* topk_w;       // [n_tok]
+  __nv_bfloat16* inter;      // [n_tok, I] bf16(silu(gate)*up)
+  float* partial;            // [n_tok, H] router-weighted fp32 partials
+  __nv_bfloat16* out;        // [M, H]
+  int32_t* counters;         // [M, H/16/R2] per-token arrival counters (zero between calls)
+  int32_t* ready;            // [E] published phase-A item passes per expert (zero between calls)
+  int32_t* sched;            // [4] next item, finished CTAs, error bits
+  int zero_rows;             // write zero rows for tokens with no local slot
+  // plan (decode_plan)
+  int NG, RP, R2, ncA, ncB, n_stages, stage_bytes, red_offset, ring_offset, smem_bytes, grid;
+};
+int decode_plan(DecodeParams& p, int sms, int max_smem);
+cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream);
+
 }  // namespace w4moe

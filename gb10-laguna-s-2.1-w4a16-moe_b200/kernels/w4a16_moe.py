@@ -85,6 +85,10 @@ def _bind(lib: ctypes.CDLL) -> None:
     lib.w4a16_last_error.argtypes = []
     lib.w4a16_version.restype = c_int
     lib.w4a16_version.argtypes = []
+    lib.w4a16_set_path.restype = c_int
+    lib.w4a16_set_path.argtypes = [c_int]
+    lib.w4a16_moe_read_status.restype = c_int
+    lib.w4a16_moe_read_status.argtypes = [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, ctypes.POINTER(ctypes.c_int32), c_vp]
     lib.w4a16_set_stage_events.restype = c_int
     lib.w4a16_set_stage_events.argtypes = [ctypes.POINTER(c_vp), c_int]
     lib.w4a16_align_buffer_len.restype = c_i64
@@ -298,6 +302,27 @@ def set_stage_events(events: list | None) -> None:
         ev.record()  # materialise the underlying cudaEvent_t
     arr = (ctypes.c_void_p * len(events))(*[ev.cuda_event for ev in events])
     _check(lib.w4a16_set_stage_events(arr, len(events)), "w4a16_set_stage_events")
+
+
+def set_path(path: str) -> None:
+    """Select the forward implementation for the calling thread: ``"auto"``
+    (fused persistent kernel for small M) or ``"general"`` (multi-kernel)."""
+    _check(load_library().w4a16_set_path({"auto": 0, "general": 1}[path]), "w4a16_set_path")
+
+
+def read_status(hidden_shape: tuple[int, int], topk: int, num_experts: int, intermediate: int,
+                device: torch.device | str = "cuda") -> int:
+    """Read and clear the error bits recorded in the pooled workspace of a
+    forward shape (0 = no bounded wait timed out).  Synchronises."""
+    M, H = hidden_shape
+    ws = _WS_CACHE.get((str(torch.device(device)), M, topk, num_experts, H, intermediate))
+    if ws is None:
+        return 0
+    out = ctypes.c_int32(0)
+    _check(load_library().w4a16_moe_read_status(_ws_ptr(ws), M, topk, num_experts, H, intermediate,
+                                                ctypes.byref(out), _stream_ptr(ws.device)),
+           "w4a16_moe_read_status")
+    return int(out.value)
 
 
 def clear_workspace_cache() -> None:

@@ -47,6 +47,22 @@ W4A16_API int w4a16_version(void);
 W4A16_API int w4a16_set_stage_events(void* const* events, int n_events);
 
 /*
+ * Path selection for the calling thread (no reference counterpart; used by
+ * tests to cover both implementations): 0 = automatic (fused persistent
+ * kernel for small M, multi-kernel path otherwise), 1 = always the
+ * multi-kernel path.
+ */
+W4A16_API int w4a16_set_path(int path);
+
+/*
+ * Reads and clears the error bits the fused kernel records in a workspace
+ * (0 = none; bit 0/1 = pipeline wait timed out, bit 2 = cross-CTA wait timed
+ * out).  Synchronises `stream`; diagnostic use only.
+ */
+W4A16_API int w4a16_moe_read_status(const void* workspace, int64_t M, int64_t topk, int64_t E,
+                                    int64_t H, int64_t I, int32_t* status_out, void* stream);
+
+/*
  * Length P of sorted_token_ids for moe_align_block_size:
  * roundup(n_tok + num_experts*(block_size-1), block_size).
  * Replaces the sizing in kernels/w4a16_moe.py:153-157 (_align_workspace).

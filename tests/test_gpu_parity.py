@@ -168,16 +168,26 @@ def _run(K, layer, hidden, tw, ids, **kw):
     return K.fused_experts_w4a16(hidden, layer["w1r"], layer["w2r"], layer["s1r"], layer["s2r"], tw, ids, **kw)
 
 
+@pytest.fixture(params=["auto", "general"])
+def path(request, K):
+    K.set_path(request.param)
+    yield request.param
+    K.set_path("auto")
+
+
 @pytest.mark.parametrize("M", [1, 4, 16, 64, 256])
-def test_forward_decode_configs(K, big_layer, M):
+def test_forward_decode_configs(K, big_layer, M, path):
     from kernels.synthetic import make_hidden, make_routing
 
     hidden = make_hidden(M, 3072, device="cuda")
     tw, ids = make_routing(M, 256, 10, device="cuda")
     out = _run(K, big_layer, hidden, tw, ids)
     torch.cuda.synchronize()
+    assert K.read_status((M, 3072), 10, 256, 1024) == 0
     ref = oracle_for(hidden, big_layer, tw, ids)
-    check_close(out, ref, None, f"M={M}")
+    check_close(out, ref, None, f"M={M} path={path}")
+    again = _run(K, big_layer, hidden, tw, ids)  # counters were left clean
+    assert torch.equal(again, out)
 
 
 @pytest.mark.parametrize("M", [1024, 4096, 16384])
