@@ -2,6 +2,7 @@
 // workspace carving and kernel dispatch.  No allocation, no host sync.
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <string>
@@ -278,6 +279,7 @@ int w4a16_moe_forward(const void* hidden, int64_t M, int64_t H, int64_t hidden_l
     dp.ready = ws.ready;
     dp.sched = ws.sched;
     dp.zero_rows = expert_map != nullptr;
+    if (const char* tr = getenv("W4A16_DECODE_TRACE")) dp.trace = (long long*)strtoull(tr, nullptr, 0);
     if (decode_plan(dp, sm_count(), max_smem_optin() - 1024)) {
       mark_stage(0, st);
       mark_stage(1, st);

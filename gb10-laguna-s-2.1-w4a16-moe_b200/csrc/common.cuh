@@ -141,14 +141,56 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the warp sleeps in hardware until the
+// phase completes or ~hint_ns elapse, instead of spinning on issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait: false after ~`budget` SM clocks (the caller records an error).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, long long budget) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_try_wait_sleep(bar, parity, 1000000u)) {
     if (clock64() - t0 > budget) return false;
   }
   return true;
+}
+
+// Same MMA without `volatile`: a pure function of its register operands, so
+// the compiler may interleave independent accumulation chains.
+__device__ __forceinline__ void mma_bf16_16816_nv(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                                  uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// (code - 8) in bf16 for the four A-fragment registers of one word (exact).
+__device__ __forceinline__ void unscaled_word(uint32_t w, uint32_t (&a)[4]) {
+  const uint32_t kMask = 0x000F000Fu, kMagic = 0x43004300u, kBias = 0x43084308u;
+  a[0] = bf16x2_sub(and_or(w, kMask, kMagic), kBias);
+  a[1] = bf16x2_sub(and_or(w >> 4, kMask, kMagic), kBias);
+  a[2] = bf16x2_sub(and_or(w >> 8, kMask, kMagic), kBias);
+  a[3] = bf16x2_sub(and_or(w >> 12, kMask, kMagic), kBias);
+}
+
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ long long global_timer_ns() {
+  long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
 }
 
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {

@@ -5,47 +5,64 @@
 // + _w4a16_moe_w1_fused_kernel + _w4a16_moe_w2_kernel + _moe_sum_kernel
 // (kernels/w4a16_moe.py:187-290, :374-670).
 //
-// Structure (one CTA per SM, 9 warps):
+// Structure (one CTA per SM; cooperative launch, so every CTA is resident):
 //   * prologue: every CTA builds the routing tables in shared memory from the
-//     raw top-k ids (histogram, scan, per-expert slot lists); no align launch.
-//   * work items, claimed dynamically from a global counter:
+//     raw top-k ids (histogram, scan, per-expert slot lists) and sizes its
+//     pipeline stages from the largest per-expert slot count.
+//   * work items, assigned round-robin (CTA b takes items b, b+grid, ...):
 //       phase A  (active expert j, RP gate/up row-tile pairs)  -> w13
 //       phase B  (active expert j, R2 hidden row tiles)        -> w2
-//     every item's K range is cut into parts that fit one pipeline stage, and
-//     an expert with more slots than one pass holds (8*NG) is done in passes.
-//   * producer warp: for each stage, cp.async.bulk of the item's weight and
-//     scale blocks (contiguous per row tile in the fragment-major layout) and
-//     of the pass's activation rows (hidden rows in phase A, intermediate rows
-//     in phase B) into a shared-memory ring; completion via mbarrier tx-count.
-//     Phase-B activation copies wait (bounded) until all phase-A items of the
-//     same expert have published their intermediate rows; the weight copies of
-//     that stage are issued before the wait, so HBM streaming never pauses at
-//     the w13 -> w2 boundary.
-//   * 8 consumer warps: decode int4 words from smem straight into m16n8k16 A
-//     fragments (scale folded in, bf16-exact like the reference's dequant),
-//     B fragments via ldmatrix, fp32 accumulation in registers; warps sharing
-//     a row tile reduce through smem at the end of an item pass.
-//   * epilogues: A writes bf16(silu(gate)*up) rows to the intermediate buffer
-//     and bumps ready[e]; B scales by the router weight, writes fp32 partials,
-//     and the last of a token's slots to finish a row block sums that token's
-//     partials in slot order (deterministic) and writes the bf16 output.
+//     all phase-A items precede all phase-B items.  An item's K range is cut
+//     into parts that fit one pipeline stage; an expert with more slots than
+//     one pass holds (8*NG) is done in passes.
+//   * producer warp: per stage, cp.async.bulk of the item's weight and scale
+//     blocks (contiguous per row tile in the fragment-major layout) and of the
+//     pass's activation rows (hidden rows in phase A, intermediate rows in
+//     phase B) into a shared-memory ring; completion via mbarrier tx-count.
+//     Phase-B activation copies wait (bounded) until every phase-A item pass
+//     of the same expert has published its intermediate rows; the weight
+//     copies of that stage are issued before the wait.  The producer shares
+//     its SM sub-partition with busy consumer warps, so stages are large
+//     (few per-stage instruction chains).
+//   * 16 consumer warps: a warp covers Rw row tiles of the item for its share
+//     of the stage's k-chunks, so each activation fragment (ldmatrix) feeds Rw
+//     tiles.  Weights are decoded from smem straight into m16n8k16 A
+//     fragments; fp32 accumulation in registers.
+//       NG == 1: A = bf16(code - 8) (exact); the bf16 group scale multiplies
+//                the fp32 partial of each 32-wide group.
+//       NG > 1:  A = bf16((code - 8) * scale), the reference's dequantised
+//                value, shared by all token groups.
+//     At the end of an item pass each warp deposits its accumulators into one
+//     of n_red reduction buffers and moves on.
+//   * epilogue warps (one per reduction buffer) reduce in fixed warp order
+//     (deterministic);
+//       A: write bf16(silu(gate) * up) rows, then bump ready[e];
+//       B: scale by the router weight and write fp32 partials; then either the
+//          last of a token's slots to finish a row block sums that token's
+//          partials in slot order (small M), or a grid-wide tail pass does.
 //   * all global counters are self-cleaning (the last CTA resets them).
+//
+// Every wait is bounded (clock64 budget); a timeout records an error bit in
+// the workspace (w4a16_moe_read_status) and the waiting warp stops.
 #include "launch.cuh"
 
 namespace w4moe {
 
-constexpr int kDecConsumers = 8;
-constexpr int kDecThreads = (kDecConsumers + 1) * 32;
+constexpr int kDecConsumers = 16;
+constexpr int kDecProducerWarp = kDecConsumers;
+constexpr int kDecEpiWarps = 4;  // epilogue warp k owns reduction buffer k (k < n_red)
+constexpr int kDecThreads = (kDecConsumers + 1 + kDecEpiWarps) * 32;
 constexpr int kDecMaxStages = 8;
 constexpr long long kWaitBudget = 4000000000LL;  // ~2 s of SM clocks
 
 // sched[] words in the workspace
-constexpr int kSchedNext = 0, kSchedDone = 1, kSchedError = 2;
+constexpr int kSchedDone = 1, kSchedError = 2, kSchedBDone = 3;
 
 enum DecodeError : int {
   kErrFullWait = 1,
   kErrEmptyWait = 2,
   kErrReadyWait = 4,
+  kErrRedWait = 8,
 };
 
 struct StageInfo {
@@ -55,15 +72,58 @@ struct StageInfo {
   int pad;
 };
 
+struct Geometry {
+  int ncA, ncB;   // chunks per stage in phase A / B
+  int rows_res;   // activation rows reserved per stage
+  int n_stages, stage_bytes;
+};
+
+// Row tiles per consumer warp: keeps Rw * NG * 4 accumulators <= 16.
+__host__ __device__ constexpr int rows_per_warp(int NG) { return NG == 4 ? 1 : 2; }
+
+// trace layout: [kind][512]; kinds 0 = producer stage issued, 1 = consumer
+// warp 0 stage data landed, 2 = consumer warp 0 stage done, 3 = epilogue 0
+// start, 4 = epilogue 0 end, 5 = kernel start / prologue end / teardown
+__device__ __forceinline__ void trace_ev(long long* tr, int kind, int k) {
+  if (tr != nullptr && blockIdx.x == 0 && k < 512) tr[kind * 512 + k] = global_timer_ns();
+}
+
 __device__ __forceinline__ void record_error(int* sched, int code) { atomicOr(sched + kSchedError, code); }
+
+__device__ __forceinline__ float bf16_lo_f32(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf16_hi_f32(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
+
+struct ItemView {
+  bool phB;
+  int q;     // row-block index within the expert
+  int e;     // local expert
+  int T;     // slots routed to e
+  int base;  // start of e's slots in the per-CTA slot list
+};
+
+__device__ __forceinline__ int stage_bytes_for(int R, int nc, int rows) {
+  return R * nc * 576 + rows * (nc * 128 + 16);
+}
+
+// Largest divisor nc of nchunks with stage bytes <= cap (0 if none).
+__device__ __forceinline__ int pick_nc(int nchunks, int R, int rows, int cap) {
+  int best = 0;
+  for (int nc = 1; nc <= nchunks; ++nc)
+    if (nchunks % nc == 0 && stage_bytes_for(R, nc, rows) <= cap) best = nc;
+  return best;
+}
 
 template <int NG>
 __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(DecodeParams p) {
   constexpr int NB = 8 * NG;
+  constexpr int RW = rows_per_warp(NG);
+  constexpr int kRedFloats = kDecConsumers * RW * NG * 128;  // one reduction buffer
   __shared__ uint64_t full_bar[kDecMaxStages], empty_bar[kDecMaxStages];
+  __shared__ uint64_t red_full[kDecEpiWarps], red_empty[kDecEpiWarps];
   __shared__ StageInfo sinfo[kDecMaxStages];
+  __shared__ StageInfo rinfo[kDecEpiWarps];
   __shared__ int s_nact;
-  __shared__ int s_last[NB];
+  __shared__ Geometry s_geo;
   extern __shared__ __align__(128) unsigned char dsm[];
 
   const int E = p.E;
@@ -72,37 +132,55 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
   int* act = off + E + 1;                  // [E]
   int* cur = act + E;                      // [E]
   int* slots = cur + E;                    // [n_tok]
-  float* red = reinterpret_cast<float*>(dsm + p.red_offset);  // [8][NG][128]
+  int* tokcnt = slots + p.n_tok;           // [M] locally routed slots per token
+  unsigned* sok = reinterpret_cast<unsigned*>(tokcnt + p.M);  // [n_tok/32+1] slot-is-local bits
+  float* red = reinterpret_cast<float*>(dsm + p.red_offset);  // [n_red][tile][warp slot][NG][128]
   unsigned char* ring = dsm + p.ring_offset;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n_red = p.n_red;
 
   // ---------------- prologue: barriers + routing tables ----------------
   if (tid == 0) {
-    for (int s = 0; s < p.n_stages; ++s) {
+    trace_ev(p.trace, 5, 0);
+    for (int s = 0; s < kDecMaxStages; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], kDecConsumers);
+    }
+    for (int b = 0; b < kDecEpiWarps; ++b) {
+      mbar_init(&red_full[b], kDecConsumers);
+      mbar_init(&red_empty[b], 1);
     }
     fence_barrier_init();
   }
   for (int e = tid; e < E; e += kDecThreads) cnt[e] = 0;
+  for (int m = tid; m < p.M; m += kDecThreads) tokcnt[m] = 0;
+  for (int w = tid; w <= p.n_tok / 32; w += kDecThreads) sok[w] = 0;
   __syncthreads();
   for (int i = tid; i < p.n_tok; i += kDecThreads) {
     const int e = p.map(i);
-    if (e >= 0) atomicAdd(&cnt[e], 1);
+    if (e >= 0) {
+      atomicAdd(&cnt[e], 1);
+      atomicAdd(&tokcnt[i / p.topk], 1);
+      atomicOr(&sok[i >> 5], 1u << (i & 31));
+    }
   }
   __syncthreads();
-  if (warp == 0) {  // exclusive scan of counts and of (count > 0)
-    int run = 0, nact = 0;
+  if (warp == 0) {  // exclusive scans of counts and of (count > 0); max count
+    int run = 0, nact = 0, mx = 0;
     for (int e0 = 0; e0 < E; e0 += 32) {
       const int e = e0 + lane;
       const int c = e < E ? cnt[e] : 0;
+      mx = max(mx, c);
       int inc = c, ia = c > 0;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int a = __shfl_up_sync(0xffffffffu, inc, o);
         const int b = __shfl_up_sync(0xffffffffu, ia, o);
-        if (lane >= o) { inc += a; ia += b; }
+        if (lane >= o) {
+          inc += a;
+          ia += b;
+        }
       }
       if (e < E) {
         off[e] = run + inc - c;
@@ -112,9 +190,21 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
       run += __shfl_sync(0xffffffffu, inc, 31);
       nact += __shfl_sync(0xffffffffu, ia, 31);
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if (lane == 0) {
       off[E] = run;
       s_nact = nact;
+      // stage geometry: the largest stages that still fit three in the ring
+      Geometry gm;
+      gm.rows_res = max(1, min(NB, mx));
+      const int cap = p.ring_bytes / 3 / 128 * 128;
+      gm.ncA = pick_nc(p.H / 64, 2 * p.RP, gm.rows_res, cap);
+      gm.ncB = pick_nc(p.I / 64, p.R2, gm.rows_res, cap);
+      gm.stage_bytes = (max(stage_bytes_for(2 * p.RP, gm.ncA, gm.rows_res),
+                            stage_bytes_for(p.R2, gm.ncB, gm.rows_res)) + 127) / 128 * 128;
+      gm.n_stages = min(kDecMaxStages, p.ring_bytes / gm.stage_bytes);
+      s_geo = gm;
     }
   }
   __syncthreads();
@@ -124,64 +214,67 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
   }
   // Expert-parallel: tokens with no local slot get a zero row.
   if (p.zero_rows) {
-    for (int m = blockIdx.x * kDecThreads + tid; m < p.M; m += gridDim.x * kDecThreads) {
-      int c = 0;
-      for (int t = 0; t < p.topk; ++t) c += p.map(m * p.topk + t) >= 0;
-      if (c == 0)
+    for (int m = blockIdx.x * kDecThreads + tid; m < p.M; m += gridDim.x * kDecThreads)
+      if (tokcnt[m] == 0)
         for (int h = 0; h < p.H; h += 8)
           *reinterpret_cast<uint4*>(p.out + (size_t)m * p.H + h) = make_uint4(0, 0, 0, 0);
-    }
   }
   __syncthreads();
+  if (tid == 0) trace_ev(p.trace, 5, 1);
 
+  const Geometry geo = s_geo;
   const int nact = s_nact;
   const int PA = (p.I / 16) / p.RP;  // phase-A items per expert
   const int PB = (p.H / 16) / p.R2;  // phase-B items per expert
   const int nA = nact * PA;
   const int total = nA + nact * PB;
   const int chA = p.H / 64, chB = p.I / 64;
-  const int partsA = chA / p.ncA, partsB = chB / p.ncB;
+  const int partsA = chA / geo.ncA, partsB = chB / geo.ncB;
+  const int S = geo.n_stages;
 
-  if (warp == kDecConsumers) {
+  auto view = [&](int item) {
+    ItemView v;
+    v.phB = item >= nA;
+    const int it = v.phB ? item - nA : item;
+    const int per = v.phB ? PB : PA;
+    const int j = it / per;
+    v.q = it - j * per;
+    v.e = act[j];
+    v.T = cnt[v.e];
+    v.base = off[v.e];
+    return v;
+  };
+
+  if (warp == kDecProducerWarp) {
     // ======================= producer warp =======================
     const uint64_t pol = l2_evict_first_policy();
     int stage = 0;
-    uint32_t uses = 0;  // total stages issued (for barrier parities)
+    uint32_t uses = 0;  // stages issued so far (barrier parities)
     bool abort = false;
-    while (!abort) {
-      int item = 0;
-      if (lane == 0) item = atomicAdd(p.sched + kSchedNext, 1);
-      item = __shfl_sync(0xffffffffu, item, 0);
+    for (int item = blockIdx.x; !abort; item += gridDim.x) {
       const bool done = item >= total;
-      const bool phB = item >= nA;
-      const int it = phB ? item - nA : item;
-      const int per = phB ? PB : PA;
-      const int j = done ? 0 : it / per, q = done ? 0 : it - (it / per) * per;
-      const int e = done ? 0 : act[j];
-      const int T = done ? 0 : cnt[e];
-      const int base = done ? 0 : off[e];
-      const int passes = done ? 1 : (T + NB - 1) / NB;
-      const int parts = done ? 1 : (phB ? partsB : partsA);
-      const int nc = phB ? p.ncB : p.ncA;
-      const int R = phB ? p.R2 : 2 * p.RP;
-      const int nchunks = phB ? chB : chA;
-      const int nrt = phB ? p.H / 16 : 2 * p.I / 16;
-      const uint8_t* wsrc = phB ? p.w2 : p.w13;
-      const uint8_t* ssrc = phB ? p.s2 : p.s13;
-      bool ready_checked = !phB;
+      ItemView v{};
+      if (!done) v = view(item);
+      const int passes = done ? 1 : (v.T + NB - 1) / NB;
+      const int parts = done ? 1 : (v.phB ? partsB : partsA);
+      const int nc = v.phB ? geo.ncB : geo.ncA;
+      const int R = v.phB ? p.R2 : 2 * p.RP;
+      const int nchunks = v.phB ? chB : chA;
+      const int nrt = v.phB ? p.H / 16 : 2 * p.I / 16;
+      const uint8_t* wsrc = v.phB ? p.w2 : p.w13;
+      const uint8_t* ssrc = v.phB ? p.s2 : p.s13;
+      const uint32_t wbytes = (uint32_t)nc * 512, sbytes = (uint32_t)nc * 64, bbytes = (uint32_t)nc * 128;
+      const int bstride = nc * 128 + 16;
+      bool ready_checked = !v.phB;
       for (int pass = 0; pass < passes && !abort; ++pass) {
+        const int rows = done ? 0 : min(NB, v.T - pass * NB);
         for (int part = 0; part < parts; ++part) {
-          if (uses >= (uint32_t)p.n_stages) {
-            const uint32_t par = ((uses / p.n_stages) - 1) & 1;
-            if (!mbar_wait(&empty_bar[stage], par, kWaitBudget)) {
-              if (lane == 0) record_error(p.sched, kErrEmptyWait);
-              abort = true;
-              break;
-            }
+          if (uses >= (uint32_t)S && !mbar_wait(&empty_bar[stage], ((uses / S) - 1) & 1, kWaitBudget)) {
+            if (lane == 0) record_error(p.sched, kErrEmptyWait);
+            abort = true;
+            break;
           }
-          unsigned char* buf = ring + (size_t)stage * p.stage_bytes;
-          const int rows = done ? 0 : min(NB, T - pass * NB);
-          const uint32_t wbytes = (uint32_t)nc * 512, sbytes = (uint32_t)nc * 64, bbytes = (uint32_t)nc * 128;
+          unsigned char* buf = ring + (size_t)stage * geo.stage_bytes;
           if (lane == 0) {
             sinfo[stage] = StageInfo{done ? -1 : item, pass, part, 0};
             const uint32_t tx = done ? 0u : (uint32_t)R * (wbytes + sbytes) + (uint32_t)rows * bbytes;
@@ -191,29 +284,30 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
           __syncwarp();
           if (!done) {
             const int c0 = part * nc;
-            // weights + scales of every row tile of the item
             for (int cpy = lane; cpy < 2 * R; cpy += 32) {
               const int r = cpy % R;
               int rt;
-              if (phB) rt = q * R + r;
-              else rt = (r < p.RP) ? q * p.RP + r : p.I / 16 + q * p.RP + (r - p.RP);
-              const size_t blk = ((size_t)e * nrt + rt) * nchunks + c0;
-              if (cpy < R) bulk_g2s_hint(buf + (size_t)r * wbytes, wsrc + blk * 512, wbytes, &full_bar[stage], pol);
-              else bulk_g2s_hint(buf + (size_t)R * wbytes + (size_t)r * sbytes, ssrc + blk * 64, sbytes,
-                                 &full_bar[stage], pol);
+              if (v.phB) rt = v.q * R + r;
+              else rt = (r < p.RP) ? v.q * p.RP + r : p.I / 16 + v.q * p.RP + (r - p.RP);
+              const size_t blk = ((size_t)v.e * nrt + rt) * nchunks + c0;
+              if (cpy < R)
+                bulk_g2s_hint(buf + (size_t)r * wbytes, wsrc + blk * 512, wbytes, &full_bar[stage], pol);
+              else
+                bulk_g2s_hint(buf + (size_t)R * wbytes + (size_t)r * sbytes, ssrc + blk * 64, sbytes,
+                              &full_bar[stage], pol);
             }
             if (!ready_checked) {
-              // intermediate rows of expert e are complete once all of its
+              // expert e's intermediate rows are complete once all of its
               // phase-A item passes have published
               if (lane == 0) {
                 const int target = PA * passes;
                 const long long t0 = clock64();
-                while (ld_acquire_gpu(p.ready + e) < target) {
+                while (ld_acquire_gpu(p.ready + v.e) < target) {
                   if (clock64() - t0 > kWaitBudget) {
                     record_error(p.sched, kErrReadyWait);
                     break;
                   }
-                  __nanosleep(64);
+                  __nanosleep(32);
                 }
               }
               __syncwarp();
@@ -221,189 +315,337 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
               ready_checked = true;
             }
             unsigned char* bdst = buf + (size_t)R * (wbytes + sbytes);
-            const int bstride = nc * 128 + 16;
             for (int rr = lane; rr < rows; rr += 32) {
-              const int slot = slots[base + pass * NB + rr];
-              const __nv_bfloat16* src =
-                  phB ? p.inter + (size_t)slot * p.I + c0 * 64
-                      : p.hidden + (size_t)(slot / p.topk) * p.hidden_ld + c0 * 64;
+              const int slot = slots[v.base + pass * NB + rr];
+              const __nv_bfloat16* src = v.phB ? p.inter + (size_t)slot * p.I + c0 * 64
+                                               : p.hidden + (size_t)(slot / p.topk) * p.hidden_ld + c0 * 64;
               bulk_g2s(bdst + (size_t)rr * bstride, src, bbytes, &full_bar[stage]);
             }
           }
+          if (lane == 0) trace_ev(p.trace, 0, (int)uses);
           ++uses;
-          stage = (stage + 1 == p.n_stages) ? 0 : stage + 1;
+          stage = (stage + 1 == S) ? 0 : stage + 1;
           if (done) break;
         }
         if (done) break;
       }
       if (done) break;
     }
-  } else {
+  } else if (warp < kDecConsumers) {
     // ======================= consumer warps =======================
     const int g = lane >> 2, t = lane & 3;
-    int stage = 0;
-    uint32_t uses = 0;
-    float acc[NG][4];
+    int stage = 0, rb = 0;
+    uint32_t uses = 0, ruses = 0;  // stages consumed; item passes handed off
+    float acc[RW][NG][4];
+    int cur_item = -1;
+    ItemView v{};
     while (true) {
-      if (!mbar_wait(&full_bar[stage], (uses / p.n_stages) & 1, kWaitBudget)) {
+      if (!mbar_wait(&full_bar[stage], (uses / S) & 1, kWaitBudget)) {
         if (lane == 0) record_error(p.sched, kErrFullWait);
         break;
       }
+      if (warp == 0 && lane == 0) trace_ev(p.trace, 1, (int)uses);
       const StageInfo si = sinfo[stage];
-      if (si.item < 0) break;
-      const bool phB = si.item >= nA;
-      const int it = phB ? si.item - nA : si.item;
-      const int per = phB ? PB : PA;
-      const int j = it / per, q = it - j * per;
-      const int e = act[j];
-      const int T = cnt[e];
-      const int base = off[e];
-      const int parts = phB ? partsB : partsA;
-      const int nc = phB ? p.ncB : p.ncA;
-      const int R = phB ? p.R2 : 2 * p.RP;
-      const int wpt = kDecConsumers / R;  // warps per row tile
-      const int r = warp / wpt, cw = warp - (warp / wpt) * wpt;
+      if (si.item < 0) {
+        // tell every epilogue warp there is nothing more
+        for (int k = 0; k < n_red; ++k) {
+          const uint32_t ru = ruses / n_red;  // earlier uses of buffer rb
+          if (ru > 0 && !mbar_wait(&red_empty[rb], (ru - 1) & 1, kWaitBudget)) {
+            if (lane == 0) record_error(p.sched, kErrRedWait);
+            break;
+          }
+          if (warp == 0 && lane == 0) rinfo[rb] = StageInfo{-1, 0, 0, 0};
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&red_full[rb]);
+          ++ruses;
+          rb = (rb + 1 == n_red) ? 0 : rb + 1;
+        }
+        break;
+      }
+      if (si.item != cur_item) {
+        v = view(si.item);
+        cur_item = si.item;
+      }
+      const int parts = v.phB ? partsB : partsA;
+      const int nc = v.phB ? geo.ncB : geo.ncA;
+      const int R = v.phB ? p.R2 : 2 * p.RP;
+      const int ngrp = R / RW;                 // tile groups per item
+      const int wpg = kDecConsumers / ngrp;    // warps per tile group
+      const int tg = warp / wpg, cw = warp - tg * wpg;
       if (si.part == 0) {
 #pragma unroll
-        for (int a = 0; a < NG; ++a)
+        for (int i = 0; i < RW; ++i)
 #pragma unroll
-          for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
+          for (int a = 0; a < NG; ++a)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) acc[i][a][b] = 0.f;
       }
-      const unsigned char* buf = ring + (size_t)stage * p.stage_bytes;
-      const unsigned char* wt = buf + (size_t)r * nc * 512;
-      const unsigned char* sc = buf + (size_t)R * nc * 512 + (size_t)r * nc * 64;
+      const unsigned char* buf = ring + (size_t)stage * geo.stage_bytes;
+      const unsigned char* wt = buf + (size_t)(tg * RW) * nc * 512 + lane * 16;
+      const unsigned char* sc = buf + (size_t)R * nc * 512 + (size_t)(tg * RW) * nc * 64 + g * 8;
       const unsigned char* bs = buf + (size_t)R * nc * 576;
       const int bstride = nc * 128 + 16;
-      const int rows = min(NB, T - si.pass * NB);
-      for (int c = cw; c < nc; c += wpt) {
-        const uint4 wv = lds128(wt + (size_t)c * 512 + lane * 16);
-        const uint2 sv = lds64(sc + (size_t)c * 64 + g * 8);
-        uint32_t A[4][4];
-        const uint32_t sg0 = __byte_perm(sv.x, 0, 0x1010), sg80 = __byte_perm(sv.x, 0, 0x3232);
-        const uint32_t sg1 = __byte_perm(sv.y, 0, 0x1010), sg81 = __byte_perm(sv.y, 0, 0x3232);
-        dequant_word(wv.x, sg0, sg80, A[0]);
-        dequant_word(wv.y, sg0, sg80, A[1]);
-        dequant_word(wv.z, sg1, sg81, A[2]);
-        dequant_word(wv.w, sg1, sg81, A[3]);
+      const int rows = min(NB, v.T - si.pass * NB);
+      const int lrow = lane & 7;
+      for (int c = cw; c < nc; c += wpg) {
+        if constexpr (NG == 1) {
+          const unsigned char* brow =
+              bs + (size_t)(lrow < geo.rows_res ? lrow : 0) * bstride + c * 128 + (lane >> 3) * 16;
+          uint32_t b0[4], b1[4];
+          ldmatrix_x4(b0, brow);
+          ldmatrix_x4(b1, brow + 64);
 #pragma unroll
-        for (int qq = 0; qq < NG; ++qq) {
-          if (qq * 8 >= rows) break;
-          const unsigned char* brow = bs + (size_t)(qq * 8 + (lane & 7)) * bstride + c * 128 + (lane >> 3) * 16;
-          uint32_t b[4];
-          ldmatrix_x4(b, brow);
-          mma_bf16_16816(acc[qq], A[0], b[0], b[1]);
-          mma_bf16_16816(acc[qq], A[1], b[2], b[3]);
-          ldmatrix_x4(b, brow + 64);
-          mma_bf16_16816(acc[qq], A[2], b[0], b[1]);
-          mma_bf16_16816(acc[qq], A[3], b[2], b[3]);
+          for (int i = 0; i < RW; ++i) {
+            const uint4 wv = lds128(wt + (size_t)(i * nc + c) * 512);
+            const uint2 sv = lds64(sc + (size_t)(i * nc + c) * 64);
+            uint32_t A0[4], A1[4], A2[4], A3[4];
+            unscaled_word(wv.x, A0);
+            unscaled_word(wv.y, A1);
+            unscaled_word(wv.z, A2);
+            unscaled_word(wv.w, A3);
+            float t0[4] = {0.f, 0.f, 0.f, 0.f}, t1[4] = {0.f, 0.f, 0.f, 0.f};
+            mma_bf16_16816_nv(t0, A0, b0[0], b0[1]);
+            mma_bf16_16816_nv(t1, A2, b1[0], b1[1]);
+            mma_bf16_16816_nv(t0, A1, b0[2], b0[3]);
+            mma_bf16_16816_nv(t1, A3, b1[2], b1[3]);
+            const float s0 = bf16_lo_f32(sv.x), s08 = bf16_hi_f32(sv.x);
+            const float s1 = bf16_lo_f32(sv.y), s18 = bf16_hi_f32(sv.y);
+            acc[i][0][0] = fmaf(s0, t0[0], fmaf(s1, t1[0], acc[i][0][0]));
+            acc[i][0][1] = fmaf(s0, t0[1], fmaf(s1, t1[1], acc[i][0][1]));
+            acc[i][0][2] = fmaf(s08, t0[2], fmaf(s18, t1[2], acc[i][0][2]));
+            acc[i][0][3] = fmaf(s08, t0[3], fmaf(s18, t1[3], acc[i][0][3]));
+          }
+        } else {
+          uint32_t A[RW][4][4];
+#pragma unroll
+          for (int i = 0; i < RW; ++i) {
+            const uint4 wv = lds128(wt + (size_t)(i * nc + c) * 512);
+            const uint2 sv = lds64(sc + (size_t)(i * nc + c) * 64);
+            const uint32_t sg0 = __byte_perm(sv.x, 0, 0x1010), sg80 = __byte_perm(sv.x, 0, 0x3232);
+            const uint32_t sg1 = __byte_perm(sv.y, 0, 0x1010), sg81 = __byte_perm(sv.y, 0, 0x3232);
+            dequant_word(wv.x, sg0, sg80, A[i][0]);
+            dequant_word(wv.y, sg0, sg80, A[i][1]);
+            dequant_word(wv.z, sg1, sg81, A[i][2]);
+            dequant_word(wv.w, sg1, sg81, A[i][3]);
+          }
+#pragma unroll
+          for (int qq = 0; qq < NG; ++qq) {
+            if (qq * 8 >= rows) break;
+            const int rr = qq * 8 + lrow;
+            const unsigned char* brow =
+                bs + (size_t)(rr < geo.rows_res ? rr : 0) * bstride + c * 128 + (lane >> 3) * 16;
+            uint32_t b0[4], b1[4];
+            ldmatrix_x4(b0, brow);
+            ldmatrix_x4(b1, brow + 64);
+#pragma unroll
+            for (int i = 0; i < RW; ++i) {
+              mma_bf16_16816_nv(acc[i][qq], A[i][0], b0[0], b0[1]);
+              mma_bf16_16816_nv(acc[i][qq], A[i][1], b0[2], b0[3]);
+              mma_bf16_16816_nv(acc[i][qq], A[i][2], b1[0], b1[1]);
+              mma_bf16_16816_nv(acc[i][qq], A[i][3], b1[2], b1[3]);
+            }
+          }
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty_bar[stage]);
+      if (warp == 0 && lane == 0) trace_ev(p.trace, 2, (int)uses);
       ++uses;
-      stage = (stage + 1 == p.n_stages) ? 0 : stage + 1;
-
+      stage = (stage + 1 == S) ? 0 : stage + 1;
       if (si.part != parts - 1) continue;
 
-      // ---------------- end of an item pass: reduce + epilogue ----------------
-      float* my = red + (size_t)warp * NG * 128;
-#pragma unroll
-      for (int qq = 0; qq < NG; ++qq) {
-        my[qq * 128 + g * 8 + 2 * t] = acc[qq][0];
-        my[qq * 128 + g * 8 + 2 * t + 1] = acc[qq][1];
-        my[qq * 128 + (g + 8) * 8 + 2 * t] = acc[qq][2];
-        my[qq * 128 + (g + 8) * 8 + 2 * t + 1] = acc[qq][3];
+      // end of an item pass: hand the accumulators to an epilogue warp
+      const uint32_t ru = ruses / n_red;
+      if (ru > 0 && !mbar_wait(&red_empty[rb], (ru - 1) & 1, kWaitBudget)) {
+        if (lane == 0) record_error(p.sched, kErrRedWait);
+        break;
       }
-      named_barrier_sync(1, kDecConsumers * 32);
-      const int ctid = tid;  // 0..255
-      if (!phB) {
+      float* rbase = red + (size_t)rb * kRedFloats;
+#pragma unroll
+      for (int i = 0; i < RW; ++i) {
+        float* my = rbase + ((size_t)((tg * RW + i) * wpg + cw) * NG) * 128;
+#pragma unroll
+        for (int qq = 0; qq < NG; ++qq) {
+          *reinterpret_cast<float2*>(my + qq * 128 + g * 8 + 2 * t) = make_float2(acc[i][qq][0], acc[i][qq][1]);
+          *reinterpret_cast<float2*>(my + qq * 128 + (g + 8) * 8 + 2 * t) =
+              make_float2(acc[i][qq][2], acc[i][qq][3]);
+        }
+      }
+      if (warp == 0 && lane == 0) rinfo[rb] = si;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&red_full[rb]);
+      ++ruses;
+      rb = (rb + 1 == n_red) ? 0 : rb + 1;
+    }
+  } else if (warp - kDecConsumers - 1 < n_red) {
+    // ======================= epilogue warps =======================
+    const int rb = warp - kDecConsumers - 1;  // this warp's reduction buffer
+    const float* rbuf = red + (size_t)rb * kRedFloats;
+    uint32_t ru = 0;
+    while (true) {
+      if (!mbar_wait(&red_full[rb], ru & 1, kWaitBudget)) {
+        if (lane == 0) record_error(p.sched, kErrRedWait);
+        break;
+      }
+      const StageInfo si = rinfo[rb];
+      if (si.item < 0) break;
+      if (rb == 0 && lane == 0) trace_ev(p.trace, 3, (int)ru);
+      const ItemView v = view(si.item);
+      const int rows = min(NB, v.T - si.pass * NB);
+      const int* sl = slots + v.base + si.pass * NB;
+      const int R = v.phB ? p.R2 : 2 * p.RP;
+      const int wpg = kDecConsumers / (R / RW);  // warp slots per tile
+      // sum over the wpg warp partials of (tile, qq), elements 4*e4 .. 4*e4+3
+      auto tile_sum4 = [&](int tile, int qq, int e4) {
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int w = 0; w < wpg; ++w) {
+          const float4 x =
+              *reinterpret_cast<const float4*>(rbuf + ((size_t)(tile * wpg + w) * NG + qq) * 128 + e4 * 4);
+          s.x += x.x;
+          s.y += x.y;
+          s.z += x.z;
+          s.w += x.w;
+        }
+        return s;
+      };
+      if (!v.phB) {
         const int RP = p.RP;
-        for (int idx = ctid; idx < RP * NG * 128; idx += kDecConsumers * 32) {
-          const int i = idx / (NG * 128), rem = idx - i * (NG * 128);
-          const int qq = rem >> 7, row = (rem >> 3) & 15, col = rem & 7;
-          const int colidx = qq * 8 + col;
-          if (colidx >= rows) continue;
-          float gs = 0.f, us = 0.f;
-          for (int w = 0; w < wpt; ++w) {
-            gs += red[((size_t)(i * wpt + w) * NG + qq) * 128 + row * 8 + col];
-            us += red[((size_t)((RP + i) * wpt + w) * NG + qq) * 128 + row * 8 + col];
+        for (int idx = lane; idx < RP * NG * 32; idx += 32) {
+          const int i = idx / (NG * 32), rem = idx - i * (NG * 32);
+          const int qq = rem >> 5, e4 = rem & 31;  // row e4/2, columns (e4&1)*4 .. +3
+          const float4 gs = tile_sum4(i, qq, e4), us = tile_sum4(RP + i, qq, e4);
+          const int row = e4 >> 1, col0 = (e4 & 1) * 4;
+          const float gv[4] = {gs.x, gs.y, gs.z, gs.w}, uv[4] = {us.x, us.y, us.z, us.w};
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            const int colidx = qq * 8 + col0 + cc;
+            if (colidx < rows)
+              p.inter[(size_t)sl[colidx] * p.I + (v.q * RP + i) * 16 + row] =
+                  __float2bfloat16(silu_f(gv[cc]) * uv[cc]);
           }
-          const int slot = slots[base + si.pass * NB + colidx];
-          p.inter[(size_t)slot * p.I + (q * RP + i) * 16 + row] = __float2bfloat16(silu_f(gs) * us);
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&red_empty[rb]);  // buffer no longer read
         __threadfence();
-        named_barrier_sync(1, kDecConsumers * 32);
-        if (ctid == 0) atomicAdd(p.ready + e, 1);
+        __syncwarp();
+        if (lane == 0) atomicAdd(p.ready + v.e, 1);
       } else {
-        const int R2 = p.R2;
-        for (int idx = ctid; idx < R2 * NG * 128; idx += kDecConsumers * 32) {
-          const int rr = idx / (NG * 128), rem = idx - rr * (NG * 128);
-          const int qq = rem >> 7, row = (rem >> 3) & 15, col = rem & 7;
-          const int colidx = qq * 8 + col;
-          if (colidx >= rows) continue;
-          float v = 0.f;
-          for (int w = 0; w < wpt; ++w) v += red[((size_t)(rr * wpt + w) * NG + qq) * 128 + row * 8 + col];
-          const int slot = slots[base + si.pass * NB + colidx];
-          p.partial[(size_t)slot * p.H + (q * R2 + rr) * 16 + row] = v * p.topk_w[slot];
-        }
-        __threadfence();
-        named_barrier_sync(1, kDecConsumers * 32);
-        if (ctid < NB) {
-          int last = -1;
-          if (ctid < rows) {
-            const int slot = slots[base + si.pass * NB + ctid];
-            const int m = slot / p.topk;
-            int valid = 0;
-            for (int tt = 0; tt < p.topk; ++tt) valid += p.map(m * p.topk + tt) >= 0;
-            int* c = p.counters + (size_t)m * PB + q;
-            if (atomicAdd(c, 1) == valid - 1) {
-              *c = 0;  // self-cleaning
-              last = m;
+        const int R2 = p.R2, span = R2 * 16;
+        for (int idx = lane; idx < R2 * NG * 32; idx += 32) {
+          const int rr = idx / (NG * 32), rem = idx - rr * (NG * 32);
+          const int qq = rem >> 5, e4 = rem & 31;
+          const float4 s4 = tile_sum4(rr, qq, e4);
+          const int row = e4 >> 1, col0 = (e4 & 1) * 4;
+          const float sv4[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            const int colidx = qq * 8 + col0 + cc;
+            if (colidx < rows) {
+              const int slot = sl[colidx];
+              p.partial[(size_t)slot * p.H + v.q * span + rr * 16 + row] = sv4[cc] * p.topk_w[slot];
             }
           }
-          s_last[ctid] = last;
         }
-        named_barrier_sync(1, kDecConsumers * 32);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&red_empty[rb]);  // buffer no longer read
         __threadfence();
-        const int span = R2 * 16;
-        for (int idx = ctid; idx < NB * span; idx += kDecConsumers * 32) {
-          const int col = idx / span, hr = idx - col * span;
-          const int m = s_last[col];
-          if (m < 0) continue;
-          float sum = 0.f;
-          for (int tt = 0; tt < p.topk; ++tt) {
-            const int slot = m * p.topk + tt;
-            if (p.map(slot) < 0) continue;
-            sum += __ldcg(p.partial + (size_t)slot * p.H + q * span + hr);
+        __syncwarp();
+        if (p.tail_reduce) {
+          if (lane == 0) atomicAdd(p.sched + kSchedBDone, 1);
+        } else {
+          // the last arriver per (token, row block) sums the token's partials
+          for (int c0 = 0; c0 < rows; c0 += 32) {
+            int mine = -1;
+            if (c0 + lane < rows) {
+              const int m = sl[c0 + lane] / p.topk;
+              int* cptr = p.counters + (size_t)m * PB + v.q;
+              if (atomicAdd(cptr, 1) == tokcnt[m] - 1) {
+                *cptr = 0;  // self-cleaning
+                mine = m;
+              }
+            }
+            unsigned todo = __ballot_sync(0xffffffffu, mine >= 0);
+            if (todo) __threadfence();
+            while (todo) {
+              const int src = __ffs(todo) - 1;
+              todo &= todo - 1;
+              const int m = __shfl_sync(0xffffffffu, mine, src);
+              for (int hr = lane; hr < span; hr += 32) {
+                const float* pp = p.partial + (size_t)m * p.topk * p.H + v.q * span + hr;
+                float sum = 0.f;
+#pragma unroll 4
+                for (int tt = 0; tt < p.topk; ++tt) {
+                  const int slot = m * p.topk + tt;
+                  const float x = __ldcg(pp + (size_t)tt * p.H);
+                  if ((sok[slot >> 5] >> (slot & 31)) & 1u) sum += x;
+                }
+                p.out[(size_t)m * p.H + v.q * span + hr] = __float2bfloat16(sum);
+              }
+            }
           }
-          p.out[(size_t)m * p.H + q * span + hr] = __float2bfloat16(sum);
         }
       }
-      named_barrier_sync(1, kDecConsumers * 32);
+      if (rb == 0 && lane == 0) trace_ev(p.trace, 4, (int)ru);
+      ++ru;
     }
   }
 
-  // ---------------- teardown: last CTA resets the global counters ----------------
+  // ---------------- tail: grid-wide top-k sum of the partials ----------------
+  // (larger M) once every phase-B item pass of every CTA has stored its
+  // partials, out[m, :] = sum over t in slot order of partial[m*topk+t, :].
+  __syncthreads();
+  if (p.tail_reduce) {
+    if (tid == 0) {
+      int target = 0;
+      for (int jj = 0; jj < nact; ++jj) target += PB * ((cnt[act[jj]] + NB - 1) / NB);
+      const long long t0 = clock64();
+      while (ld_acquire_gpu(p.sched + kSchedBDone) < target) {
+        if (clock64() - t0 > kWaitBudget) {
+          record_error(p.sched, kErrReadyWait);
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    __syncthreads();
+    const int h4 = p.H / 4;
+    const int n4 = p.M * h4;
+    for (int idx = blockIdx.x * kDecThreads + tid; idx < n4; idx += gridDim.x * kDecThreads) {
+      const int m = idx / h4, h = (idx - m * h4) * 4;
+      if (tokcnt[m] == 0) continue;
+      float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+      const float* pp = p.partial + (size_t)m * p.topk * p.H + h;
+#pragma unroll 4
+      for (int tt = 0; tt < p.topk; ++tt) {
+        const int slot = m * p.topk + tt;
+        const float4 x = __ldcg(reinterpret_cast<const float4*>(pp + (size_t)tt * p.H));
+        if ((sok[slot >> 5] >> (slot & 31)) & 1u) {
+          sum.x += x.x;
+          sum.y += x.y;
+          sum.z += x.z;
+          sum.w += x.w;
+        }
+      }
+      __nv_bfloat162 lo = __floats2bfloat162_rn(sum.x, sum.y), hi = __floats2bfloat162_rn(sum.z, sum.w);
+      uint2 pk;
+      pk.x = *reinterpret_cast<uint32_t*>(&lo);
+      pk.y = *reinterpret_cast<uint32_t*>(&hi);
+      *reinterpret_cast<uint2*>(p.out + (size_t)m * p.H + h) = pk;
+    }
+  }
+
+  // ---------------- teardown: the last CTA resets the global counters ----------------
   __syncthreads();
   if (tid == 0) {
+    trace_ev(p.trace, 5, 2);
     __threadfence();
     if (atomicAdd(p.sched + kSchedDone, 1) == (int)gridDim.x - 1) {
-      p.sched[kSchedNext] = 0;
       p.sched[kSchedDone] = 0;
+      p.sched[kSchedBDone] = 0;
       for (int e = 0; e < E; ++e) p.ready[e] = 0;
       __threadfence();
     }
   }
-}
-
-static int pick_divisor_chunks(int nchunks, int R, int NB, int slot_bytes) {
-  int best = 0;
-  for (int nc = 1; nc <= nchunks; ++nc) {
-    if (nchunks % nc) continue;
-    const long long bytes = (long long)R * nc * 576 + (long long)NB * (nc * 128 + 16);
-    if (bytes <= slot_bytes) best = nc;
-  }
-  return best;
 }
 
 int decode_plan(DecodeParams& p, int sms, int max_smem) {
@@ -411,34 +653,31 @@ int decode_plan(DecodeParams& p, int sms, int max_smem) {
   if (n_tok > kDecodeMaxSlots || p.E > 1024) return 0;
   const int max_active = n_tok < p.E ? n_tok : p.E;
   const double avg = (double)n_tok / (double)(max_active > 0 ? max_active : 1);
-  const int NG = avg <= 2.0 ? 1 : (avg <= 8.0 ? 2 : 4);
-  const int NB = 8 * NG;
+  const int NG = avg <= 1.5 ? 1 : (avg <= 6.0 ? 2 : 4);
   const int M = p.M;
   int RP = M <= 16 ? 1 : (M <= 64 ? 2 : 4);
   int R2 = M <= 16 ? 2 : (M <= 64 ? 4 : 8);
   while (RP > 1 && (p.I / 16) % RP) RP >>= 1;
   while (R2 > 2 && (p.H / 16) % R2) R2 >>= 1;
-  if ((p.H / 16) % R2) return 0;
+  if ((p.H / 16) % R2 || (p.I / 16) % RP) return 0;
+  const int RW = rows_per_warp(NG);
+  if ((2 * RP) % RW || R2 % RW) return 0;
   p.NG = NG;
   p.RP = RP;
   p.R2 = R2;
-  const int route_bytes = (4 * p.E + 1 + n_tok) * 4;
+  p.tail_reduce = M > 8;
+  const int route_bytes = (4 * p.E + 1 + n_tok + M + n_tok / 32 + 1) * 4;
   p.red_offset = (route_bytes + 127) / 128 * 128;
-  const int red_bytes = kDecConsumers * NG * 128 * 4;
-  p.ring_offset = p.red_offset + (red_bytes + 127) / 128 * 128;
-  const int avail = max_smem - p.ring_offset - 1024;  // static smem + slack
-  int stages = 6;
-  int slot = 0;
-  for (; stages >= 3; --stages) {
-    slot = (avail / stages) / 128 * 128;
-    p.ncA = pick_divisor_chunks(p.H / 64, 2 * RP, NB, slot);
-    p.ncB = pick_divisor_chunks(p.I / 64, R2, NB, slot);
-    if (p.ncA > 0 && p.ncB > 0) break;
-  }
-  if (stages < 3) return 0;
-  p.n_stages = stages;
-  p.stage_bytes = slot;
-  p.smem_bytes = p.ring_offset + stages * slot;
+  const int red_buf = kDecConsumers * RW * NG * 128 * 4;
+  p.n_red = 65536 / red_buf;
+  if (p.n_red > kDecEpiWarps) p.n_red = kDecEpiWarps;
+  if (p.n_red < 2) p.n_red = 2;
+  p.ring_offset = p.red_offset + p.n_red * red_buf;
+  p.ring_bytes = (max_smem - p.ring_offset - 1024) / 128 * 128;  // room for static smem
+  // the smallest stage (one chunk, all 8*NG rows) must fit three times
+  const int minA = 2 * RP * 576 + 8 * NG * (128 + 16), minB = R2 * 576 + 8 * NG * (128 + 16);
+  if (p.ring_bytes < 3 * (minA > minB ? minA : minB)) return 0;
+  p.smem_bytes = p.ring_offset + p.ring_bytes;
   p.grid = sms;
   return 1;
 }
@@ -455,8 +694,17 @@ cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream) {
       if (err != cudaSuccess) return err;
       configured[dev][slot] = p.smem_bytes;
     }
-    kern<<<p.grid, kDecThreads, p.smem_bytes, stream>>>(p);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.grid);
+    cfg.blockDim = dim3(kDecThreads);
+    cfg.dynamicSmemBytes = p.smem_bytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, p);
   };
   switch (p.NG) {
     case 1: return launch(moe_decode_fused_kernel<1>, 0);

@@ -83,8 +83,10 @@ struct DecodeParams {
   int32_t* ready;            // [E] published phase-A item passes per expert (zero between calls)
   int32_t* sched;            // [4] next item, finished CTAs, error bits
   int zero_rows;             // write zero rows for tokens with no local slot
-  // plan (decode_plan)
-  int NG, RP, R2, ncA, ncB, n_stages, stage_bytes, red_offset, ring_offset, smem_bytes, grid;
+  int tail_reduce;           // 1: grid-wide top-k sum after all w2 items; 0: per-token last arriver
+  long long* trace;          // optional event timestamps of CTA 0 (diagnostics; nullptr normally)
+  // plan (decode_plan); the stage geometry is derived per CTA on the device
+  int NG, RP, R2, n_red, red_offset, ring_offset, ring_bytes, smem_bytes, grid;
 };
 int decode_plan(DecodeParams& p, int sms, int max_smem);
 cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream);
