@@ -118,6 +118,18 @@ Workspace carve(char* base, int64_t M, int64_t topk, int64_t E, int64_t H, int64
 }
 
 }  // namespace
+
+// Bytes at the start of a forward workspace that must be zero before a call
+// (the self-cleaning counters); everything after them is overwritten by the call.
+int64_t workspace_zero_prefix_bytes(int64_t M, int64_t topk, int64_t E, int64_t H, int64_t I) {
+  char* const base = reinterpret_cast<char*>(static_cast<uintptr_t>(256));
+  Workspace w = carve(base, M, topk, E, H, I);
+  return reinterpret_cast<char*>(w.sorted) - base;
+}
+
+// Records `msg` as the calling thread's w4a16_last_error() and returns `code`.
+int report_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
 }  // namespace w4moe
 
 using namespace w4moe;

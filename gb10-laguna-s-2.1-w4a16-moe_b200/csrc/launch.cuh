@@ -89,6 +89,10 @@ struct DecodeParams {
   int NG, RP, R2, n_red, red_offset, ring_offset, ring_bytes, smem_bytes, grid;
 };
 int decode_plan(DecodeParams& p, int sms, int max_smem);
+
+// ---- capi.cu internals shared with other entry points ----
+int64_t workspace_zero_prefix_bytes(int64_t M, int64_t topk, int64_t E, int64_t H, int64_t I);
+int report_error(int code, const char* msg);
 cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream);
 
 }  // namespace w4moe

@@ -85,6 +85,13 @@ def _bind(lib: ctypes.CDLL) -> None:
     lib.w4a16_last_error.argtypes = []
     lib.w4a16_version.restype = c_int
     lib.w4a16_version.argtypes = []
+    lib.w4a16_moe_forward_noalloc.restype = c_int
+    lib.w4a16_moe_forward_noalloc.argtypes = [
+        c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64,
+        c_vp, c_vp, c_int, c_i64, c_vp, c_i64, c_vp, c_vp,
+    ]
+    lib.w4a16_moe_noalloc_max_workspace.restype = c_i64
+    lib.w4a16_moe_noalloc_max_workspace.argtypes = []
     lib.w4a16_set_path.restype = c_int
     lib.w4a16_set_path.argtypes = [c_int]
     lib.w4a16_moe_read_status.restype = c_int

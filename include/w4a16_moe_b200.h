@@ -119,6 +119,28 @@ W4A16_API int w4a16_moe_forward(const void* hidden, int64_t M, int64_t H, int64_
                       const int32_t* expert_map, int64_t global_num_experts, void* out,
                       void* workspace, int64_t workspace_bytes, void* stream);
 
+/*
+ * Allocation-free variant of w4a16_moe_forward (no counterpart in the
+ * reference).  For callers that may not allocate device memory where they run
+ * the layer (inside another framework's memory pool or allocator hooks, in
+ * plug-in hosts that forbid allocation on the hot path, on initialisation or
+ * error paths): same arguments minus the workspace, which is replaced by a
+ * 16 MiB static device array inside this library (held on every GPU that
+ * loads it, until exit).  Shapes needing a larger workspace are rejected with
+ * status 2.  All calls on a device share the array: calls that may overlap on
+ * the GPU race.  The first call on a device resolves the array's address
+ * (cudaGetSymbolAddress) and should come before any stream capture.
+ */
+W4A16_API int w4a16_moe_forward_noalloc(const void* hidden, int64_t M, int64_t H, int64_t hidden_ld,
+                                        const void* w13_rep, const void* s13_rep, const void* w2_rep,
+                                        const void* s2_rep, int64_t E, int64_t I,
+                                        const float* topk_weights, const void* topk_ids,
+                                        int ids_is_int64, int64_t topk, const int32_t* expert_map,
+                                        int64_t global_num_experts, void* out, void* stream);
+
+/* Size in bytes of the static scratch array behind w4a16_moe_forward_noalloc. */
+W4A16_API int64_t w4a16_moe_noalloc_max_workspace(void);
+
 #ifdef __cplusplus
 }
 #endif
