@@ -56,7 +56,7 @@ def _traffic(M: int) -> float | None:
     if not p.is_file():
         return None
     d = json.loads(p.read_text())
-    v = d.get(f"w13_M{M}")
+    v = d.get(f"decode_M{M}")
     return float(v) if v is not None else None
 
 
@@ -338,7 +338,8 @@ def run_ours(args) -> int:
 
     peaks = _peaks()
     w13_mean = sum(w13_ms) / len(w13_ms)
-    fused = sum(align_ms) < 1e-3 * len(align_ms) and sum(w2_ms) < 1e-3 * len(w2_ms)
+    # the library runs M*topk <= 4096 slots through its single fused kernel
+    fused = M * TOPK <= 4096
     if fused:  # one persistent kernel does routing + w13 + w2 + top-k sum
         kname, kbytes = "moe_decode_fused_kernel (routing + w13 + w2 + top-k sum)", wbytes
     else:
