@@ -142,7 +142,8 @@ int w4a16_version(void) { return 100; }
 
 int w4a16_set_path(int path) {
   g_last_error.clear();
-  if (path < 0 || path > 1) return fail(kInvalidArgument, "w4a16_set_path: 0 = auto, 1 = general");
+  if (path < 0 || path > 2)
+    return fail(kInvalidArgument, "w4a16_set_path: 0 = auto, 1 = general, 2 = tensor-core prefill");
   g_force_general = path;
   return kOk;
 }
@@ -326,6 +327,45 @@ int w4a16_moe_forward(const void* hidden, int64_t M, int64_t H, int64_t hidden_l
   cudaError_t err = launch_align(ap, st);
   if (err != cudaSuccess) return cuda_fail(err, "w4a16_moe_forward/align");
   mark_stage(1, st);
+
+  // Large M: tensor-core (tcgen05) grouped GEMMs + fixed-order top-k sum.
+  if (g_force_general != 1 && ((uintptr_t)hidden & 15) == 0 && (hidden_ld & 7) == 0 && I % 64 == 0 &&
+      H % 128 == 0) {
+    PrefillParams p13{};
+    p13.w = (const uint8_t*)w13_rep;
+    p13.s = (const uint8_t*)s13_rep;
+    p13.n_rowtiles = (int)(2 * I / 16);
+    p13.n_chunks = (int)(H / 64);
+    p13.x = (const __nv_bfloat16*)hidden;
+    p13.x_ld = hidden_ld;
+    p13.x_row_div = (int)topk;
+    p13.sorted = ws.sorted;
+    p13.offsets = ws.offsets;
+    p13.counts = ws.counts;
+    p13.active = ws.active;
+    p13.num_active = ws.num_active;
+    p13.E = (int)E;
+    p13.topk = (int)topk;
+    p13.I = (int)I;
+    p13.H = (int)H;
+    p13.inter = ws.inter;
+    p13.topk_w = topk_weights;
+    p13.sched = ws.sched;
+    PrefillParams p2 = p13;
+    p2.w = (const uint8_t*)w2_rep;
+    p2.s = (const uint8_t*)s2_rep;
+    p2.n_rowtiles = (int)(H / 16);
+    p2.n_chunks = (int)(I / 64);
+    p2.x = ws.inter;
+    p2.x_ld = I;
+    p2.x_row_div = 1;
+    p2.partial = (__nv_bfloat16*)ws.partial;  // bf16 partials in the fp32 partial region
+    err = launch_prefill(p13, p2, map, (int)M, (int)topk, (int)H, (__nv_bfloat16*)out, sm_count(), st);
+    if (err != cudaSuccess) return cuda_fail(err, "w4a16_moe_forward/prefill");
+    mark_stage(2, st);
+    mark_stage(3, st);
+    return kOk;
+  }
 
   const RouteView rt{ws.sorted, ws.offsets, ws.counts, ws.active, ws.num_active, ws.tok_valid};
   const int64_t max_active = n_tok < E ? n_tok : E;

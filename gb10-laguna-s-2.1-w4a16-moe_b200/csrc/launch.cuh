@@ -90,6 +90,28 @@ struct DecodeParams {
 };
 int decode_plan(DecodeParams& p, int sms, int max_smem);
 
+// ---- prefill.cu (tcgen05 grouped GEMMs for large M) ----
+struct PrefillParams {
+  const uint8_t* w;          // fragment-major weights of this projection
+  const uint8_t* s;          // scales
+  int n_rowtiles, n_chunks;  // N_out / 16, K / 64
+  const __nv_bfloat16* x;    // B-operand rows (hidden for w13, intermediate for w2)
+  long long x_ld;
+  int x_row_div;             // row of slot = slot / x_row_div
+  const int32_t* sorted;     // exact expert-sorted slot list (align, block size 1)
+  const int32_t* offsets;
+  const int32_t* counts;
+  const int32_t* active;
+  const int32_t* num_active;
+  int E, topk, I, H;
+  __nv_bfloat16* inter;      // w13 output [n_tok, I]
+  __nv_bfloat16* partial;    // w2 output [n_tok, H] (router-weighted)
+  const float* topk_w;
+  int32_t* sched;            // error bits in sched[2]
+};
+cudaError_t launch_prefill(const PrefillParams& p13, const PrefillParams& p2, const SlotMap& map, int M, int topk,
+                           int H, __nv_bfloat16* out, int sms, cudaStream_t stream);
+
 // ---- capi.cu internals shared with other entry points ----
 int64_t workspace_zero_prefix_bytes(int64_t M, int64_t topk, int64_t E, int64_t H, int64_t I);
 int report_error(int code, const char* msg);

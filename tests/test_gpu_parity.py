@@ -135,7 +135,7 @@ def _cfg0_from_golden(golden_dir):
     return c, hidden, layer, t(c["topk_weights"]), t(c["topk_ids"])
 
 
-def test_forward_config0_golden(K, golden_dir):
+def test_forward_config0_golden(K, golden_dir, path):
     c, hidden, layer, tw, ids = _cfg0_from_golden(golden_dir)
     w1r, s1r = K.repack_weights(layer["w1_q"], layer["w1_s"])
     w2r, s2r = K.repack_weights(layer["w2_q"], layer["w2_s"])
@@ -168,7 +168,7 @@ def _run(K, layer, hidden, tw, ids, **kw):
     return K.fused_experts_w4a16(hidden, layer["w1r"], layer["w2r"], layer["s1r"], layer["s2r"], tw, ids, **kw)
 
 
-@pytest.fixture(params=["auto", "general"])
+@pytest.fixture(params=["auto", "general", "prefill"])
 def path(request, K):
     K.set_path(request.param)
     yield request.param
