@@ -351,6 +351,8 @@ int w4a16_moe_forward(const void* hidden, int64_t M, int64_t H, int64_t hidden_l
     p13.inter = ws.inter;
     p13.topk_w = topk_weights;
     p13.sched = ws.sched;
+    p13.n_stages = prefill_stages((int)E, max_smem_optin());
+    if (const char* tr = getenv("W4A16_PREFILL_TRACE")) p13.trace = (long long*)strtoull(tr, nullptr, 0);
     PrefillParams p2 = p13;
     p2.w = (const uint8_t*)w2_rep;
     p2.s = (const uint8_t*)s2_rep;
@@ -360,9 +362,11 @@ int w4a16_moe_forward(const void* hidden, int64_t M, int64_t H, int64_t hidden_l
     p2.x_ld = I;
     p2.x_row_div = 1;
     p2.partial = (__nv_bfloat16*)ws.partial;  // bf16 partials in the fp32 partial region
-    err = launch_prefill(p13, p2, map, (int)M, (int)topk, (int)H, (__nv_bfloat16*)out, sm_count(), st);
-    if (err != cudaSuccess) return cuda_fail(err, "w4a16_moe_forward/prefill");
+    err = launch_prefill_w13(p13, sm_count(), st);
+    if (err != cudaSuccess) return cuda_fail(err, "w4a16_moe_forward/prefill w13");
     mark_stage(2, st);
+    err = launch_prefill_w2(p2, map, (int)M, (int)topk, (int)H, (__nv_bfloat16*)out, sm_count(), st);
+    if (err != cudaSuccess) return cuda_fail(err, "w4a16_moe_forward/prefill w2");
     mark_stage(3, st);
     return kOk;
   }

@@ -155,11 +155,15 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 }
 
 // Bounded wait: false after ~`budget` SM clocks (the caller records an error).
+// Spins with plain try_wait for ~20 us of SM clocks (phase completion is
+// seen immediately), then sleeps with a suspend hint between checks.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, long long budget) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
-  while (!mbar_try_wait_sleep(bar, parity, 1000000u)) {
-    if (clock64() - t0 > budget) return false;
+  while (!mbar_try_wait(bar, parity)) {
+    const long long dt = clock64() - t0;
+    if (dt > budget) return false;
+    if (dt > 40000 && mbar_try_wait_sleep(bar, parity, 20000u)) return true;
   }
   return true;
 }

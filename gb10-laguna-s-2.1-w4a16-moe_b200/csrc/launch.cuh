@@ -108,9 +108,13 @@ struct PrefillParams {
   __nv_bfloat16* partial;    // w2 output [n_tok, H] (router-weighted)
   const float* topk_w;
   int32_t* sched;            // error bits in sched[2]
+  int n_stages;              // pipeline depth (prefill_stages)
+  long long* trace;          // optional event timestamps of CTA 0 (diagnostics; nullptr normally)
 };
-cudaError_t launch_prefill(const PrefillParams& p13, const PrefillParams& p2, const SlotMap& map, int M, int topk,
-                           int H, __nv_bfloat16* out, int sms, cudaStream_t stream);
+int prefill_stages(int E, int max_smem_optin);
+cudaError_t launch_prefill_w13(const PrefillParams& p13, int sms, cudaStream_t stream);
+cudaError_t launch_prefill_w2(const PrefillParams& p2, const SlotMap& map, int M, int topk, int H,
+                              __nv_bfloat16* out, int sms, cudaStream_t stream);
 
 // ---- capi.cu internals shared with other entry points ----
 int64_t workspace_zero_prefix_bytes(int64_t M, int64_t topk, int64_t E, int64_t H, int64_t I);
