@@ -329,7 +329,7 @@ int w4a16_moe_forward(const void* hidden, int64_t M, int64_t H, int64_t hidden_l
   mark_stage(1, st);
 
   // Large M: tensor-core (tcgen05) grouped GEMMs + fixed-order top-k sum.
-  if (g_force_general != 1 && ((uintptr_t)hidden & 15) == 0 && (hidden_ld & 7) == 0 && I % 64 == 0 &&
+  if (g_force_general != 1 && ((uintptr_t)hidden & 15) == 0 && (hidden_ld & 7) == 0 && I % 128 == 0 &&
       H % 128 == 0) {
     PrefillParams p13{};
     p13.w = (const uint8_t*)w13_rep;
@@ -340,6 +340,11 @@ int w4a16_moe_forward(const void* hidden, int64_t M, int64_t H, int64_t hidden_l
     p13.x_ld = hidden_ld;
     p13.x_row_div = (int)topk;
     p13.sorted = ws.sorted;
+    p13.num_post = ws.num_post;
+    p13.n_tok = (int)n_tok;
+    // sorted token rows in the upper half of the partial region (the bf16
+    // partials of the w2 pass use the lower half)
+    p13.xs = (__nv_bfloat16*)ws.partial + n_tok * H;
     p13.offsets = ws.offsets;
     p13.counts = ws.counts;
     p13.active = ws.active;
@@ -354,6 +359,8 @@ int w4a16_moe_forward(const void* hidden, int64_t M, int64_t H, int64_t hidden_l
     p13.n_stages = prefill_stages((int)E, max_smem_optin());
     if (const char* tr = getenv("W4A16_PREFILL_TRACE")) p13.trace = (long long*)strtoull(tr, nullptr, 0);
     PrefillParams p2 = p13;
+    if (getenv("W4A16_PREFILL_TRACE_W2") == nullptr) p2.trace = nullptr;
+    else p13.trace = nullptr;
     p2.w = (const uint8_t*)w2_rep;
     p2.s = (const uint8_t*)s2_rep;
     p2.n_rowtiles = (int)(H / 16);

@@ -95,16 +95,19 @@ struct PrefillParams {
   const uint8_t* w;          // fragment-major weights of this projection
   const uint8_t* s;          // scales
   int n_rowtiles, n_chunks;  // N_out / 16, K / 64
-  const __nv_bfloat16* x;    // B-operand rows (hidden for w13, intermediate for w2)
+  const __nv_bfloat16* x;    // w13: hidden states (gathered into xs in sorted order)
   long long x_ld;
   int x_row_div;             // row of slot = slot / x_row_div
+  __nv_bfloat16* xs;         // w13: [n_tok, H] token rows in expert-sorted order
+  int n_tok;                 // M * topk (rows of xs / inter)
+  const int32_t* num_post;   // valid sorted positions
   const int32_t* sorted;     // exact expert-sorted slot list (align, block size 1)
   const int32_t* offsets;
   const int32_t* counts;
   const int32_t* active;
   const int32_t* num_active;
   int E, topk, I, H;
-  __nv_bfloat16* inter;      // w13 output [n_tok, I]
+  __nv_bfloat16* inter;      // w13 output [n_tok, I], rows in expert-sorted order
   __nv_bfloat16* partial;    // w2 output [n_tok, H] (router-weighted)
   const float* topk_w;
   int32_t* sched;            // error bits in sched[2]

@@ -34,41 +34,41 @@
 // an error bit in the workspace) so the kernel always terminates.
 #include <algorithm>
 
+#include <cuda.h>
+
 #include "launch.cuh"
 
 namespace w4moe {
 
 constexpr int kPfEpiWarps = 4;                        // warps 0-3: epilogue (TMEM lane quarters)
-constexpr int kPfDeqWarps = 8;                        // warps 4-11: int4 -> bf16 A tiles
-constexpr int kPfCopyWarps = 4;                       // warps 12-15: async copies
+constexpr int kPfDeqWarps = 8;                        // warps 4-11: int4 -> bf16 A tiles (2 groups)
 constexpr int kPfDeqFirst = kPfEpiWarps;
-constexpr int kPfCopyFirst = kPfDeqFirst + kPfDeqWarps;
-constexpr int kPfMmaWarp = kPfCopyFirst + kPfCopyWarps;  // warp 16: tcgen05.mma issue
-constexpr int kPfDeq = kPfDeqWarps * 32;
-constexpr int kPfCopy = kPfCopyWarps * 32;
+constexpr int kPfWLoadWarp = kPfDeqFirst + kPfDeqWarps;  // warp 12: packed-weight bulk copies
+constexpr int kPfBLoadWarp = kPfWLoadWarp + 1;           // warp 13: token-row tensor loads
+constexpr int kPfMmaWarp = kPfBLoadWarp + 1;             // warp 14: tcgen05.mma issue
+constexpr int kPfDeqGroup = kPfDeqWarps / 2 * 32;        // threads per dequant group
 constexpr int kPfThreads = (kPfMmaWarp + 1) * 32;
 constexpr int kPfStages = 4;
+constexpr int kPfWK = 2;                              // k-blocks per packed-weight stage
+constexpr int kPfWStages = 3;                         // packed-weight stages
 constexpr int kPfMaxTok = 256;                        // tokens per item (MMA N <= 256)
+constexpr int kPfBoxRows = 32;                        // token rows per tensor load
 constexpr int kPfAStage = 128 * 128;                  // 128 rows x 64 bf16
 constexpr int kPfBStage = kPfMaxTok * 128;            // 256 rows x 64 bf16
-constexpr int kPfStaging = 8 * 576;                   // 8 row tiles x (512 B + 64 B scales)
-constexpr int kPfStageBytes = kPfAStage + kPfBStage;  // 1024-aligned (staging kept apart)
-constexpr int kPfXchgCols = 16;
+constexpr int kPfStaging = kPfWK * 8 * 576;           // 8 row tiles x kPfWK x (512 B + 64 B scales)
+constexpr int kPfScaleOff = kPfWK * 8 * 512;          // scales after the packed words
+constexpr int kPfStageBytes = kPfAStage + kPfBStage;  // 1024-aligned
+constexpr int kPfXchgCols = 8;
 constexpr int kPfTmemCols = 512;
 constexpr long long kPfWaitBudget = 4000000000LL;
 
 constexpr int kPfErrWait = 16;  // error bit in sched[2]
 
-// trace layout [kind][1024] (CTA 0): 0 copies of k issued, 1 dequant saw k
-// land, 2 dequant published A(k), 3 MMA saw A(k), 4 MMA committed k
+// trace layout [kind][1024] (CTA 0): 0 token rows of k issued, 1 dequant has
+// k's weights and a free A slot, 2 dequant published A(k), 3 MMA saw A and B
+// of k, 4 MMA committed k, 5 weights of k issued
 __device__ __forceinline__ void pf_trace(long long* tr, int kind, int k) {
   if (tr != nullptr && blockIdx.x == 0 && k < 1024) tr[kind * 1024 + k] = global_timer_ns();
-}
-
-// Arrive on `bar` when all of this thread's earlier cp.async copies have landed
-// (the arrival counts toward the barrier's expected count).
-__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 struct PfItem {
@@ -76,18 +76,20 @@ struct PfItem {
 };
 
 template <int MODE>
-__global__ void __launch_bounds__(kPfThreads, 1) moe_prefill_kernel(PrefillParams p) {
+__global__ void __launch_bounds__(kPfThreads, 1)
+    moe_prefill_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tmb,
+                       const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tms) {
   extern __shared__ __align__(1024) unsigned char dsm[];
-  __shared__ uint64_t raw_full[kPfStages], a_full[kPfStages], empty_bar[kPfStages];
+  __shared__ uint64_t a_full[kPfStages], b_full[kPfStages], empty_bar[kPfStages];
+  __shared__ uint64_t w_full[kPfWStages], w_empty[kPfWStages];
   __shared__ uint64_t acc_full[2], acc_empty[2];
   __shared__ uint32_t tmem_base;
   __shared__ int s_failed, s_nact;
 
   const int S = p.n_stages;                                    // 3 or 4
   unsigned char* stages = dsm;                                 // S x (A | B), 1024-aligned
-  unsigned char* staging = dsm + S * kPfStageBytes;            // S x packed int4 blocks
-  int* rowoff = reinterpret_cast<int*>(staging + S * kPfStaging);     // [4 copy warps][256] B-row offsets
-  float* xchg = reinterpret_cast<float*>(rowoff + kPfCopyWarps * kPfMaxTok);  // [16 cols][64 rows]
+  unsigned char* wstage = dsm + S * kPfStageBytes;             // kPfWStages x packed int4 blocks
+  float* xchg = reinterpret_cast<float*>(wstage + kPfWStages * kPfStaging);  // [16 cols][64 rows]
   int* cum = reinterpret_cast<int*>(xchg + kPfXchgCols * 64);  // [E + 1]
   int* s_act = cum + p.E + 1;                                  // [E] active experts
   int* s_cnt = s_act + p.E;                                    // [E] slots per expert
@@ -100,9 +102,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) moe_prefill_kernel(PrefillParam
   // ---------------- prologue ----------------
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&raw_full[s], 32);      // the lanes of the slot's copy warp
-      mbar_init(&a_full[s], kPfDeq / 2);  // one group of 4 dequant warps
-      mbar_init(&empty_bar[s], 1);
+      mbar_init(&a_full[s], kPfDeqGroup);  // one dequant group
+      mbar_init(&b_full[s], 1);            // expect_tx of the token-row loads
+      mbar_init(&empty_bar[s], 1);         // tcgen05.commit
+    }
+    for (int s = 0; s < kPfWStages; ++s) {
+      mbar_init(&w_full[s], 1);
+      mbar_init(&w_empty[s], 2 * kPfDeqGroup);  // both dequant groups
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
@@ -180,57 +186,71 @@ __global__ void __launch_bounds__(kPfThreads, 1) moe_prefill_kernel(PrefillParam
     }
   };
 
-  if (warp >= kPfCopyFirst && warp < kPfMmaWarp) {
-    // ======================= copy warps =======================
-    // Copy warp w owns ring slot w: it fills k-blocks k = w, w+S, w+2S, ...
-    // (one cp.async commit-free stream per warp; completion is signalled per
-    // lane with cp.async.mbarrier.arrive.noinc).  Warps beyond S stay idle.
-    const int cw = warp - kPfCopyFirst;
-    int* ro = rowoff + cw * kPfMaxTok;  // this warp's B-row offsets of its current item
-    int cached_n = -1;
-    PfItem it{};
-    for (int k = cw; cw < S && k < total_k; k += S) {
-      const int n = k / nkb, kb = k - n * nkb;
-      if (n != cached_n) {
-        it = item_of(n);
-        cached_n = n;
-        for (int i = lane; i < it.ntok; i += 32)
-          ro[i] = (int)((long long)(p.sorted[it.base + i] / p.x_row_div) * p.x_ld);
-        __syncwarp();
+  auto fast_wait = [&](uint64_t* bar, uint32_t parity) {
+    if (!mbar_try_wait(bar, parity)) wait(bar, parity);
+  };
+
+  if (warp == kPfWLoadWarp) {
+    // ====== packed weights: per stage kPfWK k-blocks of 8 row tiles, 4 tensor loads ======
+    // (gate/up or hidden row tiles come in two runs of 4; smem order [tile][kb][512 B])
+    if (lane == 0) {
+      const uint32_t wbase = smem_u32(wstage);
+      int ws = 0;
+      uint32_t ph = 0;
+      bool wrapped = false;
+      for (int n = 0; n < my_items; ++n) {
+        const PfItem it = item_of(n);
+        const int row0 = it.e * p.n_rowtiles + (MODE == 0 ? it.p * 4 : it.p * 8);
+        const int row1 = MODE == 0 ? row0 + p.I / 16 : row0 + 4;
+        for (int kb = 0; kb < nkb; kb += kPfWK) {
+          if (wrapped) fast_wait(&w_empty[ws], ph ^ 1u);
+          const uint32_t stg = wbase + (uint32_t)ws * kPfStaging;
+          mbar_arrive_expect_tx(&w_full[ws], kPfStaging);
+          tma_load_3d_u32(stg, &tmw, 0, kb, row0, &w_full[ws]);
+          tma_load_3d_u32(stg + 4 * kPfWK * 512, &tmw, 0, kb, row1, &w_full[ws]);
+          tma_load_3d_u32(stg + kPfScaleOff, &tms, 0, kb, row0, &w_full[ws]);
+          tma_load_3d_u32(stg + kPfScaleOff + 4 * kPfWK * 64, &tms, 0, kb, row1, &w_full[ws]);
+          if (++ws == kPfWStages) {
+            ws = 0;
+            ph ^= 1u;
+            wrapped = true;
+          }
+        }
       }
-      const int s = cw, use = k / S;
-      if (use > 0) wait(&empty_bar[s], (use - 1) & 1);
-      if (lane == 0) pf_trace(p.trace, 5, k);
-      unsigned char* bdst = stages + (size_t)s * kPfStageBytes + kPfAStage;
-      unsigned char* stg = staging + (size_t)s * kPfStaging;
-      // packed weights + scales of the 8 row tiles: 288 16-byte granules
-      for (int gi = lane; gi < 8 * 36; gi += 32) {
-        const int i = gi / 36, q = gi - i * 36;
-        int rt;
-        if (MODE == 0) rt = (i < 4) ? it.p * 4 + i : p.I / 16 + it.p * 4 + (i - 4);
-        else rt = it.p * 8 + i;
-        const size_t blk = ((size_t)it.e * p.n_rowtiles + rt) * p.n_chunks + kb;
-        const unsigned char* src = q < 32 ? p.w + blk * 512 + q * 16 : p.s + blk * 64 + (q - 32) * 16;
-        cp_async16_zfill(stg + i * 576 + q * 16, src, true);
-      }
-      if (lane == 0) pf_trace(p.trace, 6, k);
-      // token rows (rows in [ntok, n16) keep stale values: they only reach
-      // accumulator columns that are never stored)
-      const __nv_bfloat16* xk = p.x + kb * 64;
-      for (int gi = lane; gi < it.ntok * 8; gi += 32) {
-        const int row = gi >> 3, c16 = gi & 7;
-        cp_async16_zfill(bdst + swz128(row, c16 * 8), xk + ro[row] + c16 * 8, true);
-      }
-      cp_async_arrive_noinc(&raw_full[s]);
-      if (lane == 0) pf_trace(p.trace, 0, k);
     }
-    cp_async_wait_group<0>();
-  } else if (warp >= kPfDeqFirst && warp < kPfCopyFirst) {
+    __syncwarp();
+  } else if (warp == kPfBLoadWarp) {
+    // ============ token rows: ceil(ntok / 32) tensor loads of 32 rows x 64 k ============
+    // (rows past the item belong to the next expert or are zero-filled; they
+    // only reach accumulator columns that are never stored)
+    if (lane == 0) {
+      const uint32_t bdst0 = smem_u32(stages) + kPfAStage;
+      int s = 0;
+      uint32_t ph = 0;
+      for (int n = 0; n < my_items; ++n) {
+        const PfItem it = item_of(n);
+        const int nl = (it.ntok + kPfBoxRows - 1) / kPfBoxRows;
+        const uint32_t bytes = (uint32_t)nl * kPfBoxRows * 128;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (n > 0 || kb >= S) fast_wait(&empty_bar[s], ph ^ 1u);
+          const uint32_t bdst = bdst0 + (uint32_t)s * kPfStageBytes;
+          mbar_arrive_expect_tx(&b_full[s], bytes);
+          for (int j = 0; j < nl; ++j)
+            tma_load_2d_u32(bdst + j * kPfBoxRows * 128, &tmb, kb * 64, it.base + j * kPfBoxRows, &b_full[s]);
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp >= kPfDeqFirst && warp < kPfWLoadWarp) {
     // ======================= dequant warps =======================
     // two groups of 4 warps take alternate k-blocks; a thread decodes two of
     // the eight 16-row x 64-k fragment blocks of its k-block
     const int dt = tid - kPfDeqFirst * 32;  // 0..255
-    const int grp = dt >> 7, gt = dt & 127;
+    const int grp = dt / kPfDeqGroup, gt = dt % kPfDeqGroup;
     const int fl = gt & 31, fg = fl >> 2, ft = fl & 3;
     const int fi0 = gt >> 5;  // fragment blocks fi0 and fi0 + 4
     uint32_t aoff[4][4];      // swizzled offsets for block fi0 (block fi0+4 is +64 rows = +8192 B)
@@ -243,19 +263,26 @@ __global__ void __launch_bounds__(kPfThreads, 1) moe_prefill_kernel(PrefillParam
       aoff[j][3] = swz128(r1, k0 + 8);
     }
     for (int k = grp; k < total_k; k += 2) {
-      const int s = k % S;
-      wait(&raw_full[s], (k / S) & 1);
+      const int s = k % S, use = k / S, q = k / kPfWK, ws = q % kPfWStages, sub = k % kPfWK;
+      if (use > 0) wait(&empty_bar[s], (use - 1) & 1);
+      wait(&w_full[ws], (q / kPfWStages) & 1);
       if (gt == 0) pf_trace(p.trace, 1, k);
       unsigned char* st = stages + (size_t)s * kPfStageBytes;
-      const unsigned char* stg = staging + (size_t)s * kPfStaging;
+      const unsigned char* stg = wstage + ws * kPfStaging;
+      uint4 wv[2];
+      uint2 sv[2];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const int fi = fi0 + 4 * h;
-        const uint4 wv = lds128(stg + fi * 576 + fl * 16);
-        const uint2 sv = lds64(stg + fi * 576 + 512 + fg * 8);
-        const uint32_t sg0 = __byte_perm(sv.x, 0, 0x1010), sg80 = __byte_perm(sv.x, 0, 0x3232);
-        const uint32_t sg1 = __byte_perm(sv.y, 0, 0x1010), sg81 = __byte_perm(sv.y, 0, 0x3232);
-        const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
+        const int blk = (fi0 + 4 * h) * kPfWK + sub;
+        wv[h] = lds128(stg + blk * 512 + fl * 16);
+        sv[h] = lds64(stg + kPfScaleOff + blk * 64 + fg * 8);
+      }
+      mbar_arrive(&w_empty[ws]);  // staging consumed (values are in registers)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t sg0 = __byte_perm(sv[h].x, 0, 0x1010), sg80 = __byte_perm(sv[h].x, 0, 0x3232);
+        const uint32_t sg1 = __byte_perm(sv[h].y, 0, 0x1010), sg81 = __byte_perm(sv[h].y, 0, 0x3232);
+        const uint32_t w4[4] = {wv[h].x, wv[h].y, wv[h].z, wv[h].w};
         unsigned char* sth = st + h * 8192;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -265,33 +292,45 @@ __global__ void __launch_bounds__(kPfThreads, 1) moe_prefill_kernel(PrefillParam
           for (int x = 0; x < 4; ++x) *reinterpret_cast<uint32_t*>(sth + aoff[j][x]) = a[x];
         }
       }
-      fence_proxy_async_shared();  // generic smem writes (A, and the cp.async B rows) -> tensor core
+      fence_proxy_async_shared();  // generic smem writes -> tensor-core reads
       mbar_arrive(&a_full[s]);
       if (gt == 0) pf_trace(p.trace, 2, k);
     }
   } else if (warp == kPfMmaWarp) {
     // ======================= MMA warp =======================
+    // The issuing thread's instruction stream paces the tensor pipe (a few
+    // dozen cycles per issued instruction), so the loop keeps ring positions
+    // incrementally and builds descriptors by adding to precomputed bases.
     if (lane == 0) {
+      const uint32_t sbase = smem_u32(stages);
+      const uint64_t dhi = umma_desc_sw128(sbase) - (uint64_t)((sbase >> 4) & 0x3FFF);
+      const uint32_t lo0 = (sbase >> 4) & 0x3FFF;
+      int s = 0;
+      uint32_t ph = 0, lo = lo0;
       for (int n = 0; n < my_items; ++n) {
         const PfItem it = item_of(n);
-        const int b = n & 1, use = n >> 1;
-        if (use > 0) wait(&acc_empty[b], (use - 1) & 1);
+        const int b = n & 1;
+        if (n >= 2) fast_wait(&acc_empty[b], ((n >> 1) - 1) & 1);
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(b * 256);
         const uint32_t idesc = umma_idesc_bf16(128, it.n16);
         for (int kb = 0; kb < nkb; ++kb) {
-          const int k = n * nkb + kb, s = k % S;
-          wait(&a_full[s], (k / S) & 1);
-          pf_trace(p.trace, 3, k);
+          fast_wait(&a_full[s], ph);
+          fast_wait(&b_full[s], ph);
           tc_fence_after();
-          const uint32_t a0 = smem_u32(stages + (size_t)s * kPfStageBytes);
-          const uint32_t b0 = a0 + kPfAStage;
-#pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            umma_bf16(d, umma_desc_sw128(a0 + ks * 32), umma_desc_sw128(b0 + ks * 32), idesc,
-                      (kb > 0 || ks > 0) ? 1u : 0u);
+          const uint64_t da = dhi + lo, db = dhi + lo + (kPfAStage >> 4);
+          umma_bf16(d, da, db, idesc, kb > 0 ? 1u : 0u);
+          umma_bf16(d, da + 2, db + 2, idesc, 1u);
+          umma_bf16(d, da + 4, db + 4, idesc, 1u);
+          umma_bf16(d, da + 6, db + 6, idesc, 1u);
           umma_commit(&empty_bar[s]);
-          pf_trace(p.trace, 4, k);
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+            lo = lo0;
+          } else {
+            lo += kPfStageBytes >> 4;
+          }
         }
         umma_commit(&acc_full[b]);
       }
@@ -305,12 +344,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) moe_prefill_kernel(PrefillParam
       const int b = n & 1;
       wait(&acc_full[b], (n >> 1) & 1);
       tc_fence_after();
-      const int* sl = p.sorted + it.base;  // slot of accumulator column c
       const uint32_t dbase = tmem + (uint32_t)(b * 256) + ((uint32_t)(warp * 32) << 16);
       for (int c0 = 0; c0 < it.n16; c0 += 32) {
         uint32_t v[32];
         tmem_ld32(dbase + c0, v);
         if (MODE == 0) {
+          // intermediate rows stay in expert-sorted order (the w2 pass reads
+          // them as contiguous tiles)
+          __nv_bfloat16* dst = p.inter + (size_t)(it.base + c0) * p.I + it.p * 64 + r;
 #pragma unroll
           for (int h = 0; h < 32; h += kPfXchgCols) {
             if (r >= 64) {
@@ -323,16 +364,23 @@ __global__ void __launch_bounds__(kPfThreads, 1) moe_prefill_kernel(PrefillParam
               for (int c = 0; c < kPfXchgCols; ++c) {
                 if (c0 + h + c >= it.ntok) break;
                 const float gv = __uint_as_float(v[h + c]), uv = xchg[c * 64 + r];
-                p.inter[(size_t)sl[c0 + h + c] * p.I + it.p * 64 + r] = __float2bfloat16(silu_f(gv) * uv);
+                dst[(size_t)(h + c) * p.I] = __float2bfloat16(silu_f(gv) * uv);
               }
             }
             named_barrier_sync(2, kPfEpiWarps * 32);
           }
         } else {
-          for (int c = 0; c < 32 && c0 + c < it.ntok; ++c) {
-            const int slot = sl[c0 + c];
-            p.partial[(size_t)slot * p.H + it.p * 128 + r] =
-                __float2bfloat16(__uint_as_float(v[c]) * p.topk_w[slot]);
+          // slot and router weight of column c0 + lane, broadcast per column
+          const int cl = c0 + lane;
+          const int my_slot = cl < it.ntok ? p.sorted[it.base + cl] : 0;
+          const float my_w = cl < it.ntok ? p.topk_w[my_slot] : 0.f;
+          const int ncol = min(32, it.ntok - c0);
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const int slot = __shfl_sync(0xffffffffu, my_slot, c);
+            const float wt = __shfl_sync(0xffffffffu, my_w, c);
+            if (c < ncol)
+              p.partial[(size_t)slot * p.H + it.p * 128 + r] = __float2bfloat16(__uint_as_float(v[c]) * wt);
           }
         }
       }
@@ -346,6 +394,21 @@ __global__ void __launch_bounds__(kPfThreads, 1) moe_prefill_kernel(PrefillParam
   __syncthreads();
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tmem, kPfTmemCols);
+}
+
+// xs[pos, :] = x[sorted[pos] / x_row_div, :] for pos < num_post: the w13 token
+// rows in expert-sorted order, so the GEMM reads them as contiguous tiles.
+__global__ void moe_permute_rows_kernel(const __nv_bfloat16* x, long long x_ld, int x_row_div,
+                                        const int32_t* sorted, const int32_t* num_post, int H,
+                                        __nv_bfloat16* xs) {
+  const int n = num_post[0], h8 = H / 8;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < (long long)n * h8;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int pos = (int)(idx / h8), c = (int)(idx - (long long)pos * h8) * 8;
+    const int row = sorted[pos] / x_row_div;
+    *reinterpret_cast<uint4*>(xs + (size_t)pos * H + c) =
+        *reinterpret_cast<const uint4*>(x + (size_t)row * x_ld + c);
+  }
 }
 
 // out[m, :] = bf16(sum over t in slot order of partial[m*topk + t, :]) for the
@@ -380,8 +443,7 @@ __global__ void moe_topk_sum_kernel(const __nv_bfloat16* partial, __nv_bfloat16*
 }
 
 size_t prefill_smem_bytes(int E, int stages) {
-  return (size_t)stages * (kPfStageBytes + kPfStaging) + kPfCopyWarps * kPfMaxTok * 4 + kPfXchgCols * 64 * 4 +
-         (4 * E + 1) * 4;
+  return (size_t)stages * kPfStageBytes + kPfWStages * kPfStaging + kPfXchgCols * 64 * 4 + (4 * E + 1) * 4;
 }
 
 // Pipeline depth that fits the opt-in shared memory (static smem is < 512 B).
@@ -405,10 +467,76 @@ static cudaError_t prefill_config(int E, int stages) {
   return cudaSuccess;
 }
 
+// cuTensorMapEncodeTiled, resolved through the runtime (no link-time libcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<EncodeTiledFn>(f);
+  }();
+  return fn;
+}
+
+// Tensor map over a row-major bf16 matrix [rows, cols]: boxes of 32 rows x 64
+// columns (128 B), 128-byte swizzled -- the layout of the B tiles.
+static cudaError_t rows_tmap(CUtensorMap* m, const __nv_bfloat16* base, long long rows, long long cols) {
+  EncodeTiledFn fn = encode_tiled();
+  if (fn == nullptr) return cudaErrorNotSupported;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)(rows > 0 ? rows : 1)};
+  const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  const cuuint32_t box[2] = {64, kPfBoxRows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<__nv_bfloat16*>(base), dims, strides, box,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// Tensor maps over the fragment-major weights (E * n_rowtiles, n_chunks,
+// 512 B) and scales (.., 64 B) as u32 elements: boxes of 4 row tiles x kPfWK
+// k-blocks, unswizzled.
+static cudaError_t weight_tmaps(CUtensorMap* mw, CUtensorMap* ms, const PrefillParams& p) {
+  EncodeTiledFn fn = encode_tiled();
+  if (fn == nullptr) return cudaErrorNotSupported;
+  const cuuint64_t tiles = (cuuint64_t)p.E * p.n_rowtiles, ch = (cuuint64_t)p.n_chunks;
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const cuuint64_t wd[3] = {128, ch, tiles}, wst[2] = {512, 512 * ch};
+  const cuuint32_t wb[3] = {128, kPfWK, 4};
+  CUresult r = fn(mw, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<uint8_t*>(p.w), wd, wst, wb, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  const cuuint64_t sd[3] = {16, ch, tiles}, sst[2] = {64, 64 * ch};
+  const cuuint32_t sb[3] = {16, kPfWK, 4};
+  r = fn(ms, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<uint8_t*>(p.s), sd, sst, sb, estr,
+         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 cudaError_t launch_prefill_w13(const PrefillParams& p13, int sms, cudaStream_t stream) {
   cudaError_t err = prefill_config(p13.E, p13.n_stages);
   if (err != cudaSuccess) return err;
-  moe_prefill_kernel<0><<<sms, kPfThreads, prefill_smem_bytes(p13.E, p13.n_stages), stream>>>(p13);
+  CUtensorMap tm;
+  err = rows_tmap(&tm, p13.xs, p13.n_tok, p13.H);
+  if (err != cudaSuccess) return err;
+  CUtensorMap tw, ts;
+  err = weight_tmaps(&tw, &ts, p13);
+  if (err != cudaSuccess) return err;
+  const long long work = (long long)p13.n_tok * (p13.H / 8);
+  const int blocks = (int)std::min<long long>((work + 255) / 256, (long long)sms * 8);
+  moe_permute_rows_kernel<<<blocks > 0 ? blocks : 1, 256, 0, stream>>>(p13.x, p13.x_ld, p13.x_row_div, p13.sorted,
+                                                                       p13.num_post, p13.H, p13.xs);
+  err = cudaGetLastError();
+  if (err != cudaSuccess) return err;
+  moe_prefill_kernel<0><<<sms, kPfThreads, prefill_smem_bytes(p13.E, p13.n_stages), stream>>>(p13, tm, tw, ts);
   return cudaGetLastError();
 }
 
@@ -416,7 +544,13 @@ cudaError_t launch_prefill_w2(const PrefillParams& p2, const SlotMap& map, int M
                               __nv_bfloat16* out, int sms, cudaStream_t stream) {
   cudaError_t err = prefill_config(p2.E, p2.n_stages);
   if (err != cudaSuccess) return err;
-  moe_prefill_kernel<1><<<sms, kPfThreads, prefill_smem_bytes(p2.E, p2.n_stages), stream>>>(p2);
+  CUtensorMap tm;
+  err = rows_tmap(&tm, p2.inter, p2.n_tok, p2.I);
+  if (err != cudaSuccess) return err;
+  CUtensorMap tw, ts;
+  err = weight_tmaps(&tw, &ts, p2);
+  if (err != cudaSuccess) return err;
+  moe_prefill_kernel<1><<<sms, kPfThreads, prefill_smem_bytes(p2.E, p2.n_stages), stream>>>(p2, tm, tw, ts);
   err = cudaGetLastError();
   if (err != cudaSuccess) return err;
   const long long work = (long long)M * (H / 8);
