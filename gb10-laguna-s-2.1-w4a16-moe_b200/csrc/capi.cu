@@ -5,6 +5,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <string>
 
 #include "../../include/w4a16_moe_b200.h"
@@ -82,7 +83,7 @@ constexpr int64_t kMaxAlignBlock = 128;
 
 struct Workspace {
   int32_t *counts, *offsets, *active, *num_active, *num_post, *tok_valid;
-  int32_t *sorted, *expert_ids, *counters, *ready, *sched;
+  int32_t *sorted, *expert_ids, *counters, *ready, *sched, *align_bar;
   __nv_bfloat16* inter;
   float* partial;
   int64_t bytes;
@@ -103,6 +104,7 @@ Workspace carve(char* base, int64_t M, int64_t topk, int64_t E, int64_t H, int64
   w.counters = (int32_t*)take(4 * M * (H / 32));
   w.ready = (int32_t*)take(4 * E);
   w.sched = (int32_t*)take(4 * 4);
+  w.align_bar = (int32_t*)take(4 * 4);
   w.counts = (int32_t*)take(4 * E);
   w.offsets = (int32_t*)take(4 * (E + 1));
   w.active = (int32_t*)take(4 * E);
@@ -176,9 +178,23 @@ int64_t w4a16_align_buffer_len(int64_t n_tok, int64_t num_experts, int64_t block
   return align_up(n_tok + num_experts * (block_size - 1), block_size);
 }
 
+int64_t w4a16_moe_align_scratch_bytes(int64_t n_tok, int64_t num_experts) {
+  if (n_tok < 0 || num_experts <= 0 || num_experts > 1024) return -1;
+  if (align_grid_ctas((int)std::min<int64_t>(n_tok, 1LL << 30), (int)num_experts, sm_count()) == 0) return 0;
+  return 256 + 4 * (int64_t)align_grid_scratch_ints((int)num_experts, sm_count());
+}
+
 int w4a16_moe_align(const void* topk_ids, int ids_is_int64, int64_t M, int64_t topk,
                     int64_t num_experts, int64_t block_size, int32_t* sorted_token_ids,
                     int32_t* expert_ids, int32_t* num_tokens_post_padded, void* stream) {
+  return w4a16_moe_align_ex(topk_ids, ids_is_int64, M, topk, num_experts, block_size, sorted_token_ids,
+                            expert_ids, num_tokens_post_padded, nullptr, 0, stream);
+}
+
+int w4a16_moe_align_ex(const void* topk_ids, int ids_is_int64, int64_t M, int64_t topk,
+                       int64_t num_experts, int64_t block_size, int32_t* sorted_token_ids,
+                       int32_t* expert_ids, int32_t* num_tokens_post_padded, void* scratch,
+                       int64_t scratch_bytes, void* stream) {
   g_last_error.clear();
   if (M < 0 || topk <= 0 || num_experts <= 0 || block_size <= 0)
     return fail(kInvalidArgument, "w4a16_moe_align: bad sizes M=%lld topk=%lld E=%lld bs=%lld",
@@ -199,7 +215,15 @@ int w4a16_moe_align(const void* topk_ids, int ids_is_int64, int64_t M, int64_t t
   p.sorted = sorted_token_ids;
   p.expert_ids = expert_ids;
   p.num_post = num_tokens_post_padded;
-  cudaError_t err = launch_align(p, (cudaStream_t)stream);
+  cudaError_t err;
+  const int ctas = scratch != nullptr ? align_grid_ctas(p.n_tok, p.E, sm_count()) : 0;
+  if (ctas > 0 && scratch_bytes >= w4a16_moe_align_scratch_bytes(p.n_tok, p.E)) {
+    p.grid_bar = (int32_t*)scratch;
+    p.scratch = (int32_t*)((char*)scratch + 256);
+    err = launch_align_grid(p, ctas, (cudaStream_t)stream);
+  } else {
+    err = launch_align(p, (cudaStream_t)stream);
+  }
   if (err != cudaSuccess) return cuda_fail(err, "w4a16_moe_align");
   return kOk;
 }
@@ -324,7 +348,17 @@ int w4a16_moe_forward(const void* hidden, int64_t M, int64_t H, int64_t hidden_l
   ap.zero_rows = (__nv_bfloat16*)out;
   ap.H = (int)H;
   mark_stage(0, st);
-  cudaError_t err = launch_align(ap, st);
+  cudaError_t err;
+  // chunk totals of the multi-CTA align live in the partial region (free
+  // until the GEMMs run)
+  const int align_ctas = align_grid_ctas((int)n_tok, (int)E, sm_count());
+  if (align_ctas > 0 && (int64_t)align_grid_scratch_ints((int)E, sm_count()) * 4 <= 4 * n_tok * H) {
+    ap.scratch = (int32_t*)ws.partial;
+    ap.grid_bar = ws.align_bar;
+    err = launch_align_grid(ap, align_ctas, st);
+  } else {
+    err = launch_align(ap, st);
+  }
   if (err != cudaSuccess) return cuda_fail(err, "w4a16_moe_forward/align");
   mark_stage(1, st);
 

@@ -24,8 +24,14 @@ struct AlignParams {
   int32_t* tok_valid;       // [n_tok/topk]
   __nv_bfloat16* zero_rows; // [M, H] rows zeroed where tok_valid == 0
   int H;
+  // multi-CTA variant only
+  int32_t* scratch;         // [C * E] chunk totals
+  int32_t* grid_bar;        // [3] zero-initialised: arrivals, generation, error word
 };
 cudaError_t launch_align(const AlignParams& p, cudaStream_t stream);
+int align_grid_ctas(int n_tok, int E, int sms);
+size_t align_grid_scratch_ints(int E, int sms);
+cudaError_t launch_align_grid(const AlignParams& p, int ctas, cudaStream_t stream);
 
 // ---- repack.cu ----
 struct RepackParams {

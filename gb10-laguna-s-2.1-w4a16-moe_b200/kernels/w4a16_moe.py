@@ -102,6 +102,10 @@ def _bind(lib: ctypes.CDLL) -> None:
     lib.w4a16_align_buffer_len.argtypes = [c_i64, c_i64, c_i64]
     lib.w4a16_moe_align.restype = c_int
     lib.w4a16_moe_align.argtypes = [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp]
+    lib.w4a16_moe_align_scratch_bytes.restype = c_i64
+    lib.w4a16_moe_align_scratch_bytes.argtypes = [c_i64, c_i64]
+    lib.w4a16_moe_align_ex.restype = c_int
+    lib.w4a16_moe_align_ex.argtypes = [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp]
     lib.w4a16_repack.restype = c_int
     lib.w4a16_repack.argtypes = [c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp]
     lib.w4a16_moe_workspace_size.restype = c_i64
@@ -250,10 +254,14 @@ def moe_align_block_size(
     if bufs is None:
         P = int(lib.w4a16_align_buffer_len(n_tok, num_experts, block_size))
         assert P >= 0, "bad align sizes"
+        with torch.cuda.device(device):
+            sb = int(lib.w4a16_moe_align_scratch_bytes(n_tok, num_experts))
         bufs = (
             torch.empty(P, dtype=torch.int32, device=device),
             torch.empty(P // block_size, dtype=torch.int32, device=device),
             torch.empty(1, dtype=torch.int32, device=device),
+            # multi-CTA scratch (zero-filled once, left clean by every call)
+            torch.zeros(max(sb, 0) + 256, dtype=torch.uint8, device=device) if sb > 0 else None,
         )
         _ALIGN_CACHE[key] = bufs
     ids = topk_ids
@@ -262,14 +270,16 @@ def moe_align_block_size(
     ids = ids.contiguous()
     with torch.cuda.device(device):
         _check(
-            lib.w4a16_moe_align(
+            lib.w4a16_moe_align_ex(
                 ids.data_ptr(), 1 if ids.dtype == torch.int64 else 0, M, topk, num_experts,
                 block_size, bufs[0].data_ptr(), bufs[1].data_ptr(), bufs[2].data_ptr(),
+                _ws_ptr(bufs[3]) if bufs[3] is not None else None,
+                bufs[3].numel() - 256 if bufs[3] is not None else 0,
                 _stream_ptr(device),
             ),
             "w4a16_moe_align",
         )
-    return bufs
+    return bufs[:3]
 
 
 # ---------------------------------------------------------------------------

@@ -83,6 +83,20 @@ W4A16_API int w4a16_moe_align(const void* topk_ids, int ids_is_int64, int64_t M,
                     int32_t* expert_ids, int32_t* num_tokens_post_padded, void* stream);
 
 /*
+ * Same outputs as w4a16_moe_align, with caller-provided scratch that lets
+ * large inputs run as one multi-CTA cooperative kernel instead of one CTA
+ * (no reference counterpart).  scratch: w4a16_moe_align_scratch_bytes()
+ * bytes, 256-byte aligned, zero-filled once before its first use and left
+ * clean by every call; calls sharing one scratch must be stream-ordered.
+ * With scratch == NULL or a size of 0 this is w4a16_moe_align.
+ */
+W4A16_API int64_t w4a16_moe_align_scratch_bytes(int64_t n_tok, int64_t num_experts);
+W4A16_API int w4a16_moe_align_ex(const void* topk_ids, int ids_is_int64, int64_t M, int64_t topk,
+                    int64_t num_experts, int64_t block_size, int32_t* sorted_token_ids,
+                    int32_t* expert_ids, int32_t* num_tokens_post_padded, void* scratch,
+                    int64_t scratch_bytes, void* stream);
+
+/*
  * Load-time weight transform into this library's fragment-major layout.
  * Replaces repack_weights (kernels/w4a16_moe.py:63-116).
  *   w_q     (E, N_out, K/2) uint8        scales (E, N_out, K/group_size) bf16
