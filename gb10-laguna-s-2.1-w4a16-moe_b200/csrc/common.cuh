@@ -297,6 +297,12 @@ __device__ __forceinline__ void tma_load_2d_u32(uint32_t dst, const void* tmap, 
       : "memory");
 }
 
+// L2 prefetch of a 2-D tensor box (no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(tmap), "r"(x), "r"(y)
+               : "memory");
+}
+
 // 3-D tiled tensor load (TMA) of box at {x, y, z} completing on `bar`.
 __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int x, int y, int z, uint64_t* bar) {
   asm volatile(

@@ -52,7 +52,8 @@ constexpr int kPfStages = 4;
 constexpr int kPfWK = 2;                              // k-blocks per packed-weight stage
 constexpr int kPfWStages = 3;                         // packed-weight stages
 constexpr int kPfMaxTok = 256;                        // tokens per item (MMA N <= 256)
-constexpr int kPfBoxRows = 32;                        // token rows per tensor load
+constexpr int kPfBoxRows = 32;
+constexpr int kPfPrefetch = 8;                        // token-row k-blocks prefetched into L2 ahead                        // token rows per tensor load
 constexpr int kPfAStage = 128 * 128;                  // 128 rows x 64 bf16
 constexpr int kPfBStage = kPfMaxTok * 128;            // 256 rows x 64 bf16
 constexpr int kPfStaging = kPfWK * 8 * 576;           // 8 row tiles x kPfWK x (512 B + 64 B scales)
@@ -71,13 +72,20 @@ __device__ __forceinline__ void pf_trace(long long* tr, int kind, int k) {
   if (tr != nullptr && blockIdx.x == 0 && k < 1024) tr[kind * 1024 + k] = global_timer_ns();
 }
 
+// Token-row tensor maps with box heights 32, 64, ..., 256 rows: each k-block's
+// rows arrive with a single tensor load (the per-load cost is ~45 SM clocks,
+// comparable to streaming 3 KB).
+struct PfRowMaps {
+  CUtensorMap m[kPfMaxTok / kPfBoxRows];
+};
+
 struct PfItem {
   int e, p, chunk, ntok, n16, base;
 };
 
 template <int MODE>
 __global__ void __launch_bounds__(kPfThreads, 1)
-    moe_prefill_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tmb,
+    moe_prefill_kernel(const PrefillParams p, const __grid_constant__ PfRowMaps tmb,
                        const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tms) {
   extern __shared__ __align__(1024) unsigned char dsm[];
   __shared__ uint64_t a_full[kPfStages], b_full[kPfStages], empty_bar[kPfStages];
@@ -210,6 +218,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           tma_load_3d_u32(stg + 4 * kPfWK * 512, &tmw, 0, kb, row1, &w_full[ws]);
           tma_load_3d_u32(stg + kPfScaleOff, &tms, 0, kb, row0, &w_full[ws]);
           tma_load_3d_u32(stg + kPfScaleOff + 4 * kPfWK * 64, &tms, 0, kb, row1, &w_full[ws]);
+          if (p.trace != nullptr) pf_trace(p.trace, 5, n * nkb + kb);
           if (++ws == kPfWStages) {
             ws = 0;
             ph ^= 1u;
@@ -231,12 +240,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const PfItem it = item_of(n);
         const int nl = (it.ntok + kPfBoxRows - 1) / kPfBoxRows;
         const uint32_t bytes = (uint32_t)nl * kPfBoxRows * 128;
+        const CUtensorMap* bm = &tmb.m[nl - 1];  // box of nl * 32 rows: one load per k-block
         for (int kb = 0; kb < nkb; ++kb) {
           if (n > 0 || kb >= S) fast_wait(&empty_bar[s], ph ^ 1u);
           const uint32_t bdst = bdst0 + (uint32_t)s * kPfStageBytes;
           mbar_arrive_expect_tx(&b_full[s], bytes);
-          for (int j = 0; j < nl; ++j)
-            tma_load_2d_u32(bdst + j * kPfBoxRows * 128, &tmb, kb * 64, it.base + j * kPfBoxRows, &b_full[s]);
+          tma_load_2d_u32(bdst, bm, kb * 64, it.base, &b_full[s]);
+          if (p.trace != nullptr) pf_trace(p.trace, 0, n * nkb + kb);
           if (++s == S) {
             s = 0;
             ph ^= 1u;
@@ -314,9 +324,22 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(b * 256);
         const uint32_t idesc = umma_idesc_bf16(128, it.n16);
-        for (int kb = 0; kb < nkb; ++kb) {
+        // k-blocks are consumed in pairs: each readiness check of the issuing
+        // thread costs several hundred cycles once MMAs are in flight, so
+        // checking two stages at once keeps the tensor pipe fed (nkb is even)
+        for (int kb = 0; kb < nkb; kb += 2) {
+          int s1 = s + 1;
+          uint32_t ph1 = ph, lo1 = lo + (kPfStageBytes >> 4);
+          if (s1 == S) {
+            s1 = 0;
+            ph1 ^= 1u;
+            lo1 = lo0;
+          }
           fast_wait(&a_full[s], ph);
           fast_wait(&b_full[s], ph);
+          fast_wait(&a_full[s1], ph1);
+          fast_wait(&b_full[s1], ph1);
+          if (p.trace != nullptr) pf_trace(p.trace, 3, n * nkb + kb);
           tc_fence_after();
           const uint64_t da = dhi + lo, db = dhi + lo + (kPfAStage >> 4);
           umma_bf16(d, da, db, idesc, kb > 0 ? 1u : 0u);
@@ -324,15 +347,23 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           umma_bf16(d, da + 4, db + 4, idesc, 1u);
           umma_bf16(d, da + 6, db + 6, idesc, 1u);
           umma_commit(&empty_bar[s]);
-          if (++s == S) {
+          const uint64_t da1 = dhi + lo1, db1 = dhi + lo1 + (kPfAStage >> 4);
+          umma_bf16(d, da1, db1, idesc, 1u);
+          umma_bf16(d, da1 + 2, db1 + 2, idesc, 1u);
+          umma_bf16(d, da1 + 4, db1 + 4, idesc, 1u);
+          umma_bf16(d, da1 + 6, db1 + 6, idesc, 1u);
+          umma_commit(&empty_bar[s1]);
+          s = s1 + 1;
+          ph = ph1;
+          lo = lo1 + (kPfStageBytes >> 4);
+          if (s == S) {
             s = 0;
             ph ^= 1u;
             lo = lo0;
-          } else {
-            lo += kPfStageBytes >> 4;
           }
         }
         umma_commit(&acc_full[b]);
+        if (p.trace != nullptr) pf_trace(p.trace, 4, n);
       }
     }
     __syncwarp();
@@ -386,6 +417,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[b]);
+      if (p.trace != nullptr && tid == 0) pf_trace(p.trace, 6, n);
     }
   }
 
@@ -484,19 +516,22 @@ static EncodeTiledFn encode_tiled() {
   return fn;
 }
 
-// Tensor map over a row-major bf16 matrix [rows, cols]: boxes of 32 rows x 64
-// columns (128 B), 128-byte swizzled -- the layout of the B tiles.
-static cudaError_t rows_tmap(CUtensorMap* m, const __nv_bfloat16* base, long long rows, long long cols) {
+// Tensor maps over a row-major bf16 matrix [rows, cols]: boxes of 64 columns
+// (128 B) x (32 * (i + 1)) rows, 128-byte swizzled -- the layout of the B tiles.
+static cudaError_t rows_tmaps(PfRowMaps* maps, const __nv_bfloat16* base, long long rows, long long cols) {
   EncodeTiledFn fn = encode_tiled();
   if (fn == nullptr) return cudaErrorNotSupported;
   const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)(rows > 0 ? rows : 1)};
   const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-  const cuuint32_t box[2] = {64, kPfBoxRows};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<__nv_bfloat16*>(base), dims, strides, box,
-                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+  for (int i = 0; i < kPfMaxTok / kPfBoxRows; ++i) {
+    const cuuint32_t box[2] = {64, (cuuint32_t)(kPfBoxRows * (i + 1))};
+    const CUresult r = fn(&maps->m[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<__nv_bfloat16*>(base), dims,
+                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  }
+  return cudaSuccess;
 }
 
 // Tensor maps over the fragment-major weights (E * n_rowtiles, n_chunks,
@@ -524,8 +559,8 @@ static cudaError_t weight_tmaps(CUtensorMap* mw, CUtensorMap* ms, const PrefillP
 cudaError_t launch_prefill_w13(const PrefillParams& p13, int sms, cudaStream_t stream) {
   cudaError_t err = prefill_config(p13.E, p13.n_stages);
   if (err != cudaSuccess) return err;
-  CUtensorMap tm;
-  err = rows_tmap(&tm, p13.xs, p13.n_tok, p13.H);
+  PfRowMaps tm;
+  err = rows_tmaps(&tm, p13.xs, p13.n_tok, p13.H);
   if (err != cudaSuccess) return err;
   CUtensorMap tw, ts;
   err = weight_tmaps(&tw, &ts, p13);
@@ -544,8 +579,8 @@ cudaError_t launch_prefill_w2(const PrefillParams& p2, const SlotMap& map, int M
                               __nv_bfloat16* out, int sms, cudaStream_t stream) {
   cudaError_t err = prefill_config(p2.E, p2.n_stages);
   if (err != cudaSuccess) return err;
-  CUtensorMap tm;
-  err = rows_tmap(&tm, p2.inter, p2.n_tok, p2.I);
+  PfRowMaps tm;
+  err = rows_tmaps(&tm, p2.inter, p2.n_tok, p2.I);
   if (err != cudaSuccess) return err;
   CUtensorMap tw, ts;
   err = weight_tmaps(&tw, &ts, p2);
