@@ -364,7 +364,7 @@ int w4a16_moe_forward(const void* hidden, int64_t M, int64_t H, int64_t hidden_l
 
   // Large M: tensor-core (tcgen05) grouped GEMMs + fixed-order top-k sum.
   if (g_force_general != 1 && ((uintptr_t)hidden & 15) == 0 && (hidden_ld & 7) == 0 && I % 128 == 0 &&
-      H % 128 == 0) {
+      H % 128 == 0 && prefill_stages((int)E, max_smem_optin()) > 0) {
     PrefillParams p13{};
     p13.w = (const uint8_t*)w13_rep;
     p13.s = (const uint8_t*)s13_rep;

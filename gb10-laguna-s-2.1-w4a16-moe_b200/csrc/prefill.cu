@@ -52,8 +52,7 @@ constexpr int kPfStages = 4;
 constexpr int kPfWK = 2;                              // k-blocks per packed-weight stage
 constexpr int kPfWStages = 3;                         // packed-weight stages
 constexpr int kPfMaxTok = 256;                        // tokens per item (MMA N <= 256)
-constexpr int kPfBoxRows = 32;
-constexpr int kPfPrefetch = 8;                        // token-row k-blocks prefetched into L2 ahead                        // token rows per tensor load
+constexpr int kPfBoxRows = 32;                        // granularity of the token-row tensor loads
 constexpr int kPfAStage = 128 * 128;                  // 128 rows x 64 bf16
 constexpr int kPfBStage = kPfMaxTok * 128;            // 256 rows x 64 bf16
 constexpr int kPfStaging = kPfWK * 8 * 576;           // 8 row tiles x kPfWK x (512 B + 64 B scales)
@@ -61,7 +60,7 @@ constexpr int kPfScaleOff = kPfWK * 8 * 512;          // scales after the packed
 constexpr int kPfStageBytes = kPfAStage + kPfBStage;  // 1024-aligned
 constexpr int kPfXchgCols = 8;
 constexpr int kPfTmemCols = 512;
-constexpr long long kPfWaitBudget = 4000000000LL;
+constexpr long long kPfWaitBudget = 1000000000LL;  // SM clocks (~0.5 s)
 
 constexpr int kPfErrWait = 16;  // error bit in sched[2]
 
