@@ -11,6 +11,12 @@ metric, bench/bench_moe.py:250-263, :742-743).  Each step is replayed from a
 CUDA graph (as the reference's --cudagraph mode) with a 256 MiB L2 flush
 before it, outside the timed events.
 
+``--workload ep`` runs benchmark configuration 4 instead: a stack of four
+such layers, expert-parallel over the N ranks (E/N experts and their weights
+per rank), M=8192 tokens per step split evenly over the ranks as source
+batches, Zipf(1.1)-biased top-10 routing, NCCL all-to-all dispatch and
+combine; ``value`` is tokens/s of the whole job.
+
 ``--impl reference`` times the reference algorithm's CPU path (the numpy
 oracle port; the reference itself is PyTorch and cannot travel to the GPU box)
 on all host cores, same config and metric.  With N>1 GPUs every rank runs its
@@ -383,8 +389,134 @@ def run_ours(args) -> int:
                                  "kernel times from event-bracketed eager launches of the same steps"},
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "us_per_step": 1e3 * e2e_total / args.steps},
-            "gpu_launches": (1 if fused else 4) * args.steps,
+            "gpu_launches": (1 if fused else 5) * args.steps,
             "roofline": roofline,
+            "cpu_baseline": cpu,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+
+EP_LAYERS, EP_TOKENS = 4, 8192
+FLOP_PER_SLOT = 2 * (2 * I * H + H * I)
+
+
+def run_ep(args) -> int:
+    """Benchmark configuration 4: expert-parallel 4-layer stack, M=8192 per step."""
+    import torch
+
+    from kernels import ep
+    from kernels import w4a16_moe as K
+    from kernels.synthetic import make_hidden, make_layer, make_routing, zipf_bias
+
+    world, rank, local = _dist()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    K.load_library()
+    assert EP_TOKENS % world == 0 and E % world == 0
+    m_src = EP_TOKENS // world
+    own = ep.owned_experts(E, world, rank)
+    emap = ep.local_expert_map(E, world, rank, dev)
+    bias = zipf_bias(E, 1.1, seed=0)
+    layers, routing = [], []
+    for l in range(EP_LAYERS):
+        lay = make_layer(len(own), H, I, seed=1000 * l + rank, device=dev)  # this rank's experts only
+        w1r, s1r = K.repack_weights(lay["w1_q"], lay["w1_s"])
+        w2r, s2r = K.repack_weights(lay["w2_q"], lay["w2_s"])
+        del lay
+        layers.append(ep.LocalExperts(w1r, s1r, w2r, s2r))
+        tw, ids = make_routing(m_src, E, TOPK, seed=7919 * l + 31 * rank, device=dev, bias=bias)
+        routing.append((tw, ids))
+    x0 = make_hidden(m_src, H, seed=rank, device=dev)
+
+    def step(x):
+        for l in range(EP_LAYERS):
+            x = ep.moe_layer(x, routing[l][0], routing[l][1], layers[l], E, emap)
+        return x
+
+    for _ in range(max(args.warmup, 3)):
+        step(x0)
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        t0.record()
+        for _ in range(args.steps):
+            out = step(x0)
+        t1.record()
+        t1.synchronize()
+    _barrier(world)
+    my_ms = t0.elapsed_time(t1)
+    total_ms = _max_over_ranks(my_ms, world)
+    value = EP_TOKENS * args.steps / (total_ms * 1e-3)
+
+    # rows this rank sends per step (dispatch + combine each move them once)
+    sent_rows = 0
+    for l in range(EP_LAYERS):
+        pl = ep.plan(routing[l][1], E)
+        sent_rows += sum(c for r, c in enumerate(pl.send_counts) if r != rank)
+    nvlink_bytes = 2 * sent_rows * H * 2
+    max_sent = _max_over_ranks(float(nvlink_bytes), world)
+
+    # ---- end to end: source tokens from pinned host memory, result back ----
+    x_host = x0.cpu().pin_memory()
+    out_host = torch.empty((m_src, H), dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty_like(x0)
+    _barrier(world)
+    torch.cuda.synchronize()
+    t0.record()
+    for _ in range(args.steps):
+        xd.copy_(x_host, non_blocking=True)
+        o = step(xd)
+        out_host.copy_(o, non_blocking=True)
+    t1.record()
+    t1.synchronize()
+    e2e_ms = _max_over_ranks(t0.elapsed_time(t1), world)
+    assert torch.isfinite(out.float()).all()
+
+    peaks = _peaks()
+    flops = EP_LAYERS * EP_TOKENS * TOPK * FLOP_PER_SLOT  # whole job per step
+    per_gpu_tflops = flops / world / (total_ms / args.steps * 1e-3) / 1e12
+    ms_step = total_ms / args.steps
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import moe_oracle as O  # noqa: F401  (checker only)
+        sub_tok = 4
+        lay0 = make_layer(E, H, I, seed=0, device=dev)
+        tw_s, ids_s = routing[0][0][:sub_tok], routing[0][1][:sub_tok]
+        subl, lid = routed_layer_to_cpu(lay0, ids_s)
+        del lay0
+        per, n = cpu_port_time(sub_tok, subl, x0[:sub_tok].cpu(), tw_s.cpu(), lid.cpu(), 1, args.cpu_budget, 1000)
+        cpu = {"value": sub_tok / per / EP_LAYERS, "unit": "tokens/s", "cores": 1, "kind": "port",
+               "sample": f"{n} numpy-oracle forwards of one layer for {sub_tok} tokens (per-call dequant of "
+                         f"their routed experts), scaled to the 4-layer stack, 1 thread"}
+    if rank == 0:
+        line = {
+            "metric": "ep_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config 4: expert-parallel stack of 4 MoE layers (E=256 top-10 H=3072 I=1024 "
+                                   "int4 g32), 8192 tokens per step, Zipf(1.1)-biased routing",
+                       "tokens_per_step": EP_TOKENS, "layers": EP_LAYERS, "experts_per_rank": len(own),
+                       "parallelism": f"ep{world}",
+                       "l2": "inputs larger than L2 (each layer's expert weights stream from HBM)",
+                       "timing": "CUDA events around all steps on each rank, max over ranks",
+                       "nvlink_bytes_per_step_max_rank": max_sent},
+            "e2e": {"value": EP_TOKENS * args.steps / (e2e_ms * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": m_src * H * 2, "d2h_bytes_per_step": m_src * H * 2,
+                    "ms_per_step": e2e_ms / args.steps},
+            "gpu_launches": EP_LAYERS * 8 * args.steps,
+            "roofline": {"bound": "tensor", "achieved": per_gpu_tflops, "peak": peaks["bf16_tflops_sustained"],
+                         "unit": "TFLOP/s", "frac": per_gpu_tflops / peaks["bf16_tflops_sustained"],
+                         "traffic": None, "kernel": "whole expert-parallel step (per GPU)",
+                         "peak_src": f"{peaks['src']} bf16_tflops_sustained"},
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),
         }
@@ -405,11 +537,15 @@ def main(argv=None) -> int:
     ap.add_argument("--M", type=int, default=1, help="tokens per step (config 1: 1)")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline sampling")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["decode", "ep"], default="decode",
+                    help="decode: configs 1-3 (--M); ep: config 4, expert-parallel over the ranks")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.workload == "ep":
+        return run_ep(args)
     return run_ours(args)
 
 

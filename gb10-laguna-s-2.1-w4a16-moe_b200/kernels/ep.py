@@ -1,0 +1,196 @@
+"""Expert-parallel W4A16 MoE layers over ``torch.distributed`` (NCCL on GPUs).
+
+The reference runs one GPU and has no expert parallelism; vLLM's EP contract
+(``expert_map`` / ``global_num_experts`` in ``apply()``,
+compressed_tensors_moe_wna16.py) is what :func:`fused_experts_w4a16` accepts,
+and this module builds the token exchange around it:
+
+* rank ``r`` of ``G`` owns experts ``[r*E/G, (r+1)*E/G)`` and only their
+  repacked weights;
+* each source token is sent once to every rank that owns one of its top-k
+  experts (deduplicated per rank, not per slot), with its top-k ids and
+  weights (:func:`plan`, ``w4a16_ep_plan`` / ``w4a16_ep_pack``);
+* the owner runs :func:`fused_experts_w4a16` with its ``expert_map`` over the
+  received rows -- slots of other ranks' experts contribute nothing -- and
+  returns one bf16 row per (token, owner rank);
+* the source sums those rows in rank order in fp32 (``w4a16_ep_combine``).
+
+Collectives: one ``all_to_all_single`` of the per-rank counts (read back to the
+host for the split sizes), then rows + routing metadata out and result rows
+back.  :func:`exchange` is plain ``torch.distributed`` and runs on ``gloo``
+ranks on CPU as well.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from kernels import w4a16_moe as _K
+
+_BOUND = False
+
+
+def _lib() -> ctypes.CDLL:
+    global _BOUND
+    lib = _K.load_library()
+    if not _BOUND:
+        c_i64, c_int, c_vp = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p
+        lib.w4a16_ep_plan.restype = c_int
+        lib.w4a16_ep_plan.argtypes = [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp]
+        lib.w4a16_ep_pack.restype = c_int
+        lib.w4a16_ep_pack.argtypes = [c_vp, c_i64, c_vp, c_int, c_vp, c_i64, c_i64, c_i64, c_i64,
+                                      c_vp, c_vp, c_vp, c_vp, c_vp]
+        lib.w4a16_ep_combine.restype = c_int
+        lib.w4a16_ep_combine.argtypes = [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp]
+        _BOUND = True
+    return lib
+
+
+def owned_experts(num_experts: int, world: int, rank: int) -> range:
+    """Global ids of the experts rank ``rank`` owns (contiguous, E % G == 0)."""
+    assert num_experts % world == 0, "experts must divide evenly over ranks"
+    per = num_experts // world
+    return range(rank * per, (rank + 1) * per)
+
+
+def local_expert_map(num_experts: int, world: int, rank: int, device) -> torch.Tensor:
+    """vLLM-style ``expert_map``: global id -> local id, or -1 if not owned."""
+    emap = torch.full((num_experts,), -1, dtype=torch.int32)
+    r = owned_experts(num_experts, world, rank)
+    emap[r.start:r.stop] = torch.arange(len(r), dtype=torch.int32)
+    return emap.to(device)
+
+
+def exchange(send: torch.Tensor, send_counts: list[int], recv_counts: list[int], group=None) -> torch.Tensor:
+    """All-to-all-v of rows: ``send`` holds ``send_counts[r]`` rows for rank r
+    (rank-major); returns the rows received, ``recv_counts[r]`` from rank r."""
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    if world == 1:
+        return send[: send_counts[0]]
+    recv = send.new_empty((sum(recv_counts),) + tuple(send.shape[1:]))
+    dist.all_to_all_single(recv, send[: sum(send_counts)].contiguous(), recv_counts, send_counts, group=group)
+    return recv
+
+
+def exchange_counts(send_counts: torch.Tensor, group=None) -> torch.Tensor:
+    """Counts each rank will receive from every rank (transpose of the send counts)."""
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    if world == 1:
+        return send_counts.clone()
+    recv = torch.empty_like(send_counts)
+    dist.all_to_all_single(recv, send_counts, group=group)
+    return recv
+
+
+@dataclass
+class Plan:
+    """Send layout of one source batch (device tensors + host split sizes)."""
+
+    send_counts: list[int]
+    recv_counts: list[int]
+    offsets: torch.Tensor  # [G+1] int32, rank-major send order
+    send_tok: torch.Tensor  # [M*G] int32, token of each send row
+    tok_row: torch.Tensor  # [M*G] int32, send row of (token, rank) or -1
+
+
+def plan(topk_ids: torch.Tensor, num_experts: int, group=None) -> Plan:
+    """Destination ranks per token (GPU kernel), then the count exchange."""
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    M, topk = topk_ids.shape
+    dev = topk_ids.device
+    ids = topk_ids if topk_ids.dtype in (torch.int32, torch.int64) else topk_ids.to(torch.int32)
+    ids = ids.contiguous()
+    counts = torch.empty(world, dtype=torch.int32, device=dev)
+    offsets = torch.empty(world + 1, dtype=torch.int32, device=dev)
+    send_tok = torch.empty(max(M * world, 1), dtype=torch.int32, device=dev)
+    tok_row = torch.empty(max(M * world, 1), dtype=torch.int32, device=dev)
+    lib = _lib()
+    with torch.cuda.device(dev):
+        _K._check(
+            lib.w4a16_ep_plan(ids.data_ptr(), 1 if ids.dtype == torch.int64 else 0, M, topk, num_experts, world,
+                              counts.data_ptr(), offsets.data_ptr(), send_tok.data_ptr(), tok_row.data_ptr(),
+                              _K._stream_ptr(dev)),
+            "w4a16_ep_plan",
+        )
+    recv = exchange_counts(counts, group)
+    return Plan(counts.tolist(), recv.tolist(), offsets, send_tok, tok_row)
+
+
+def pack(hidden: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor, pl: Plan):
+    """Rows and routing metadata in send order: (x_send [n,H] bf16, meta [n,2k] int32)."""
+    M, H = hidden.shape
+    topk = topk_ids.shape[1]
+    world = len(pl.send_counts)
+    n = sum(pl.send_counts)
+    dev = hidden.device
+    x_send = torch.empty((max(n, 1), H), dtype=torch.bfloat16, device=dev)
+    meta = torch.empty((max(n, 1), 2 * topk), dtype=torch.int32, device=dev)
+    ids = topk_ids if topk_ids.dtype in (torch.int32, torch.int64) else topk_ids.to(torch.int32)
+    ids = ids.contiguous()
+    tw = topk_weights.to(torch.float32).contiguous()
+    if hidden.stride(1) != 1:
+        hidden = hidden.contiguous()
+    with torch.cuda.device(dev):
+        _K._check(
+            _lib().w4a16_ep_pack(hidden.data_ptr(), hidden.stride(0), ids.data_ptr(),
+                                 1 if ids.dtype == torch.int64 else 0, tw.data_ptr(), M, topk, H, world,
+                                 pl.offsets.data_ptr(), pl.send_tok.data_ptr(), x_send.data_ptr(), meta.data_ptr(),
+                                 _K._stream_ptr(dev)),
+            "w4a16_ep_pack",
+        )
+    return x_send[:n], meta[:n]
+
+
+def combine(back: torch.Tensor, tok_row: torch.Tensor, M: int, world: int, H: int) -> torch.Tensor:
+    """out[m] = bf16(sum over owner ranks, in rank order, of the returned rows)."""
+    out = torch.empty((M, H), dtype=torch.bfloat16, device=tok_row.device)
+    if M == 0:
+        return out
+    if back.shape[0] == 0:  # nothing was sent anywhere: every row is zero
+        back = out.new_zeros((1, H))
+    with torch.cuda.device(out.device):
+        _K._check(
+            _lib().w4a16_ep_combine(back.data_ptr(), tok_row.data_ptr(), M, world, H, out.data_ptr(),
+                                    _K._stream_ptr(out.device)),
+            "w4a16_ep_combine",
+        )
+    return out
+
+
+@dataclass
+class LocalExperts:
+    """This rank's repacked weights of one layer (experts owned_experts(E, G, rank))."""
+
+    w13: torch.Tensor
+    s13: torch.Tensor
+    w2: torch.Tensor
+    s2: torch.Tensor
+
+
+def moe_layer(hidden: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor, experts: LocalExperts,
+              num_experts: int, expert_map: torch.Tensor, group=None) -> torch.Tensor:
+    """One expert-parallel MoE layer for this rank's source tokens.
+
+    ``topk_ids`` hold global expert ids.  Returns ``[M, H]`` bf16: the same
+    result as a single-GPU :func:`fused_experts_w4a16` over all experts, up to
+    the bf16 rounding of each owner rank's partial sum.
+    """
+    M, H = hidden.shape
+    pl = plan(topk_ids, num_experts, group)
+    x_send, meta_send = pack(hidden, topk_weights, topk_ids, pl)
+    x_recv = exchange(x_send, pl.send_counts, pl.recv_counts, group)
+    meta_recv = exchange(meta_send, pl.send_counts, pl.recv_counts, group)
+    topk = topk_ids.shape[1]
+    if x_recv.shape[0] > 0:
+        ids_recv = meta_recv[:, :topk].contiguous()
+        w_recv = meta_recv[:, topk:].contiguous().view(torch.float32)
+        y = _K.fused_experts_w4a16(x_recv, experts.w13, experts.w2, experts.s13, experts.s2, w_recv, ids_recv,
+                                   expert_map=expert_map, global_num_experts=num_experts)
+    else:
+        y = x_recv.new_empty((0, H))
+    back = exchange(y, pl.recv_counts, pl.send_counts, group)
+    return combine(back, pl.tok_row, M, len(pl.send_counts), H)

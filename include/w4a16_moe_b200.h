@@ -155,6 +155,32 @@ W4A16_API int w4a16_moe_forward_noalloc(const void* hidden, int64_t M, int64_t H
 /* Size in bytes of the static scratch array behind w4a16_moe_forward_noalloc. */
 W4A16_API int64_t w4a16_moe_noalloc_max_workspace(void);
 
+/*
+ * Expert-parallel token exchange (no counterpart in the reference, which runs
+ * on one GPU; these serve vLLM's expert_map / global_num_experts contract).
+ * Rank r of G owns experts [r*E/G, (r+1)*E/G); E % G == 0.
+ *
+ * w4a16_ep_plan: per source token, the ranks owning any of its top-k experts.
+ *   send_counts [G], send_offsets [G+1] (rank-major send order, tokens
+ *   ascending inside a rank), send_tok [<= M*G] (token of each send row),
+ *   tok_row [M*G] (send row of (token m, rank r) or -1).
+ * w4a16_ep_pack: gathers hidden rows and their routing into send order:
+ *   x_send [n_send, H] bf16, meta_send [n_send, 2*topk] int32 = top-k ids
+ *   then the fp32 bit patterns of the top-k weights; n_send = send_offsets[G]
+ *   is read on the device (buffers sized M*G rows).
+ * w4a16_ep_combine: out[m] = bf16(sum over r ascending of back[tok_row[m,r]])
+ *   in fp32; rows with no destination are zero.  back [n_send, H] bf16.
+ */
+W4A16_API int w4a16_ep_plan(const void* topk_ids, int ids_is_int64, int64_t M, int64_t topk,
+                    int64_t num_experts, int64_t n_ranks, int32_t* send_counts,
+                    int32_t* send_offsets, int32_t* send_tok, int32_t* tok_row, void* stream);
+W4A16_API int w4a16_ep_pack(const void* hidden, int64_t hidden_ld, const void* topk_ids, int ids_is_int64,
+                    const float* topk_weights, int64_t M, int64_t topk, int64_t H, int64_t n_ranks,
+                    const int32_t* send_offsets, const int32_t* send_tok, void* x_send,
+                    int32_t* meta_send, void* stream);
+W4A16_API int w4a16_ep_combine(const void* back, const int32_t* tok_row, int64_t M, int64_t n_ranks,
+                    int64_t H, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
