@@ -320,7 +320,9 @@ int w4a16_moe_forward(const void* hidden, int64_t M, int64_t H, int64_t hidden_l
     if (decode_plan(dp, sm_count(), max_smem_optin() - 1024)) {
       mark_stage(0, st);
       mark_stage(1, st);
-      cudaError_t err = launch_decode(dp, st);
+      static const bool staged_only = getenv("W4A16_DECODE_STAGED") != nullptr;  // A/B comparisons
+      cudaError_t err = (!staged_only && decode_direct_ok(dp, max_smem_optin() - 1024)) ? launch_decode_direct(dp, st)
+                                                                                         : launch_decode(dp, st);
       if (err != cudaSuccess) return cuda_fail(err, "w4a16_moe_forward/decode");
       mark_stage(2, st);
       mark_stage(3, st);

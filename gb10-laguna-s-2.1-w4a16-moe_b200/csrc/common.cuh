@@ -401,6 +401,27 @@ struct SlotMap {
   }
 };
 
+// Per-expert slot lists in ascending slot order, identical in every CTA that
+// builds them (an atomic scatter would order slots differently per CTA, and
+// CTAs that split one expert's slots into passes must agree on the split).
+// One warp; eid[i] = local expert of slot i or -1; cur[e] = first position of
+// expert e (advanced past its slots on return).
+__device__ __forceinline__ void ordered_slot_scatter(const int* eid, int n_tok, int* cur, int* slots, int lane) {
+  const unsigned lt = (1u << lane) - 1u;
+  for (int i0 = 0; i0 < n_tok; i0 += 32) {
+    const int i = i0 + lane;
+    const int e = i < n_tok ? eid[i] : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int leader = __ffs(peers) - 1;
+    int base = (e >= 0 && lane == leader) ? cur[e] : 0;
+    base = __shfl_sync(0xffffffffu, base, leader);
+    if (e >= 0) slots[base + __popc(peers & lt)] = i;
+    __syncwarp();
+    if (e >= 0 && lane == leader) cur[e] = base + __popc(peers);
+    __syncwarp();
+  }
+}
+
 // Routing arrays derived once per forward by the align kernel and consumed by
 // the GEMM kernels.  All live in the caller-provided workspace.
 struct RouteView {

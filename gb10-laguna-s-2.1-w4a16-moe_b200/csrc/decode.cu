@@ -44,6 +44,8 @@
 //
 // Every wait is bounded (clock64 budget); a timeout records an error bit in
 // the workspace (w4a16_moe_read_status) and the waiting warp stops.
+#include <stdlib.h>
+
 #include "launch.cuh"
 
 namespace w4moe {
@@ -134,6 +136,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
   int* slots = cur + E;                    // [n_tok]
   int* tokcnt = slots + p.n_tok;           // [M] locally routed slots per token
   unsigned* sok = reinterpret_cast<unsigned*>(tokcnt + p.M);  // [n_tok/32+1] slot-is-local bits
+  int* eid = reinterpret_cast<int*>(sok + p.n_tok / 32 + 1);   // [n_tok] local expert per slot
   float* red = reinterpret_cast<float*>(dsm + p.red_offset);  // [n_red][tile][warp slot][NG][128]
   unsigned char* ring = dsm + p.ring_offset;
 
@@ -159,6 +162,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
   __syncthreads();
   for (int i = tid; i < p.n_tok; i += kDecThreads) {
     const int e = p.map(i);
+    eid[i] = e;
     if (e >= 0) {
       atomicAdd(&cnt[e], 1);
       atomicAdd(&tokcnt[i / p.topk], 1);
@@ -198,7 +202,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
       // stage geometry: the largest stages that still fit three in the ring
       Geometry gm;
       gm.rows_res = max(1, min(NB, mx));
-      const int cap = p.ring_bytes / 3 / 128 * 128;
+      const int cap = p.ring_bytes / p.ring_div / 128 * 128;
       gm.ncA = pick_nc(p.H / 64, 2 * p.RP, gm.rows_res, cap);
       gm.ncB = pick_nc(p.I / 64, p.R2, gm.rows_res, cap);
       gm.stage_bytes = (max(stage_bytes_for(2 * p.RP, gm.ncA, gm.rows_res),
@@ -208,10 +212,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
     }
   }
   __syncthreads();
-  for (int i = tid; i < p.n_tok; i += kDecThreads) {
-    const int e = p.map(i);
-    if (e >= 0) slots[atomicAdd(&cur[e], 1)] = i;
-  }
+  if (warp == 0) ordered_slot_scatter(eid, p.n_tok, cur, slots, lane);
   // Expert-parallel: tokens with no local slot get a zero row.
   if (p.zero_rows) {
     for (int m = blockIdx.x * kDecThreads + tid; m < p.M; m += gridDim.x * kDecThreads)
@@ -666,7 +667,7 @@ int decode_plan(DecodeParams& p, int sms, int max_smem) {
   p.RP = RP;
   p.R2 = R2;
   p.tail_reduce = M > 8;
-  const int route_bytes = (4 * p.E + 1 + n_tok + M + n_tok / 32 + 1) * 4;
+  const int route_bytes = (4 * p.E + 1 + 2 * n_tok + M + n_tok / 32 + 1) * 4;
   p.red_offset = (route_bytes + 127) / 128 * 128;
   const int red_buf = kDecConsumers * RW * NG * 128 * 4;
   p.n_red = 65536 / red_buf;
@@ -679,6 +680,13 @@ int decode_plan(DecodeParams& p, int sms, int max_smem) {
   if (p.ring_bytes < 3 * (minA > minB ? minA : minB)) return 0;
   p.smem_bytes = p.ring_offset + p.ring_bytes;
   p.grid = sms;
+  if (p.ring_div <= 0) {
+    static const int env_div = [] {
+      const char* e = getenv("W4A16_DECODE_RING_DIV");
+      return e ? atoi(e) : 0;
+    }();
+    p.ring_div = env_div > 0 ? env_div : 3;
+  }
   return 1;
 }
 

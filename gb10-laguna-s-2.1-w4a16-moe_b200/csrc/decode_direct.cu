@@ -1,0 +1,390 @@
+// Fused small-M MoE layer for the fewest-tokens-per-expert regime (at most
+// ~1.5 routed slots per active expert, e.g. M = 1 .. ~20 at top-10 of 256):
+// routing + w13 (+SiLU*up) + w2 (+ router-weighted top-k sum) in one
+// persistent cooperative kernel in which every warp streams its own weights.
+//
+// Replaces, in that regime, the reference's moe_align_block_size +
+// _w4a16_moe_w1_fused_kernel + _w4a16_moe_w2_kernel + _moe_sum_kernel
+// (kernels/w4a16_moe.py:187-290, :374-670).
+//
+// Why a second decode kernel: with one or two tokens per expert the layer is a
+// pure weight stream (53 MB at M = 1) and the staged design (a producer warp
+// filling a shared-memory ring for 16 consumer warps, per-item reductions by
+// epilogue warps) spends its time in per-stage handshakes.  Here there is no
+// producer, ring or epilogue warp:
+//   * units: w13 (expert, pass of <= 8 tokens, gate/up row-tile pair, K half)
+//            and w2 (expert, pass, 32-row block); all w13 units precede all
+//            w2 units; warp g of the grid takes units g, g + warps, ...
+//   * a warp loads its unit's fragment-major weight and scale blocks straight
+//     from global memory into registers, kPfD chunks (64 k) ahead, decodes
+//     int4 -> bf16 (code - 8, exact) into m16n8k16 A fragments and multiplies
+//     with the tokens' activations (B fragments loaded from global / L1); the
+//     bf16 group scales multiply the fp32 partial of each 32-wide group;
+//   * w13: the two K halves of a pair run on adjacent warps of one CTA and meet
+//     in shared memory; the first writes bf16(silu(gate) * up) and bumps the
+//     expert's readiness counter;
+//   * w2: a unit prefetches its first weight chunks, waits (bounded) until the
+//     expert's w13 pairs have all published, multiplies by the router weight
+//     into fp32 partials, and the last unit to finish a (token, row block)
+//     sums that token's partials in slot order (deterministic).
+// Every wait is bounded; counters are self-cleaning.
+#include "launch.cuh"
+
+namespace w4moe {
+
+constexpr int kDdWarps = 16;
+constexpr int kDdThreads = kDdWarps * 32;
+constexpr int kDdNB = 8;       // tokens per pass (one n8 MMA column block)
+constexpr int kDdD = 3;        // weight chunks in flight per warp
+constexpr int kDdSplitA = 2;   // K halves per w13 gate/up pair
+constexpr long long kDdBudget = 2000000000LL;  // SM clocks
+
+// sched[] words shared with the staged decode kernel
+constexpr int kDdSchedDone = 1, kDdSchedError = 2;
+constexpr int kDdErrReady = 4;
+
+struct DdChunk {
+  uint4 w[2];   // two row tiles' fragment words
+  uint2 s[2];   // their group scales
+};
+
+__device__ __forceinline__ float dd_lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float dd_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
+
+// acc[4] (C fragment of one row tile) += scale-weighted MMA of one 64-k chunk.
+__device__ __forceinline__ void dd_chunk_mma(float (&acc)[4], const uint4& wv, const uint2& sv,
+                                             const uint32_t (&b)[8]) {
+  uint32_t A0[4], A1[4], A2[4], A3[4];
+  unscaled_word(wv.x, A0);
+  unscaled_word(wv.y, A1);
+  unscaled_word(wv.z, A2);
+  unscaled_word(wv.w, A3);
+  float t0[4] = {0.f, 0.f, 0.f, 0.f}, t1[4] = {0.f, 0.f, 0.f, 0.f};
+  mma_bf16_16816_nv(t0, A0, b[0], b[1]);
+  mma_bf16_16816_nv(t1, A2, b[4], b[5]);
+  mma_bf16_16816_nv(t0, A1, b[2], b[3]);
+  mma_bf16_16816_nv(t1, A3, b[6], b[7]);
+  const float s0 = dd_lo(sv.x), s08 = dd_hi(sv.x), s1 = dd_lo(sv.y), s18 = dd_hi(sv.y);
+  acc[0] = fmaf(s0, t0[0], fmaf(s1, t1[0], acc[0]));
+  acc[1] = fmaf(s0, t0[1], fmaf(s1, t1[1], acc[1]));
+  acc[2] = fmaf(s08, t0[2], fmaf(s18, t1[2], acc[2]));
+  acc[3] = fmaf(s08, t0[3], fmaf(s18, t1[3], acc[3]));
+}
+
+// B fragments of one 64-k chunk for this lane's token row (k16 steps 0..3).
+template <bool CG>
+__device__ __forceinline__ void dd_load_b(uint32_t (&b)[8], const __nv_bfloat16* row, int c, int t) {
+  const uint32_t* p = reinterpret_cast<const uint32_t*>(row + c * 64) + t;
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    if (CG) {
+      b[2 * s] = __ldcg(p + s * 8);
+      b[2 * s + 1] = __ldcg(p + s * 8 + 4);
+    } else {
+      b[2 * s] = __ldg(p + s * 8);
+      b[2 * s + 1] = __ldg(p + s * 8 + 4);
+    }
+  }
+}
+
+__device__ __forceinline__ void dd_load_chunk(DdChunk& ch, const uint8_t* w, const uint8_t* s, size_t blk0,
+                                              size_t blk1, int lane, int g) {
+  ch.w[0] = ldg_stream(reinterpret_cast<const uint4*>(w + blk0 * 512) + lane);
+  ch.w[1] = ldg_stream(reinterpret_cast<const uint4*>(w + blk1 * 512) + lane);
+  ch.s[0] = __ldg(reinterpret_cast<const uint2*>(s + blk0 * 64) + g);
+  ch.s[1] = __ldg(reinterpret_cast<const uint2*>(s + blk1 * 64) + g);
+}
+
+__global__ void __launch_bounds__(kDdThreads, 1) moe_decode_direct_kernel(DecodeParams p) {
+  extern __shared__ __align__(16) int dd_smem[];
+  __shared__ float xchg[kDdWarps / 2][8][32];  // w13 K-half partials (gate 4 + up 4 per lane)
+  __shared__ int s_nact, s_nA, s_nB;
+
+  const int E = p.E;
+  int* cnt = dd_smem;                 // [E]
+  int* off = cnt + E;                 // [E+1]
+  int* act = off + E + 1;             // [E]
+  int* cur = act + E;                 // [E]
+  int* cumP = cur + E;                // [E+1] prefix of passes over active experts
+  int* slots = cumP + E + 1;          // [n_tok]
+  int* tokcnt = slots + p.n_tok;      // [M]
+  unsigned* sok = reinterpret_cast<unsigned*>(tokcnt + p.M);  // [n_tok/32+1]
+  int* eid = reinterpret_cast<int*>(sok + p.n_tok / 32 + 1);   // [n_tok] local expert per slot
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t = lane & 3;
+
+  // ---------------- routing tables (every CTA builds its own copy) ----------------
+  for (int e = tid; e < E; e += kDdThreads) cnt[e] = 0;
+  for (int m = tid; m < p.M; m += kDdThreads) tokcnt[m] = 0;
+  for (int w = tid; w <= p.n_tok / 32; w += kDdThreads) sok[w] = 0;
+  __syncthreads();
+  for (int i = tid; i < p.n_tok; i += kDdThreads) {
+    const int e = p.map(i);
+    eid[i] = e;
+    if (e >= 0) {
+      atomicAdd(&cnt[e], 1);
+      atomicAdd(&tokcnt[i / p.topk], 1);
+      atomicOr(&sok[i >> 5], 1u << (i & 31));
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int run = 0, nact = 0, runP = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int e = e0 + lane;
+      const int c = e < E ? cnt[e] : 0;
+      const int pc = (c + kDdNB - 1) / kDdNB;
+      int inc = c, ia = c > 0, ip = pc;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int a = __shfl_up_sync(0xffffffffu, inc, o);
+        const int b = __shfl_up_sync(0xffffffffu, ia, o);
+        const int d = __shfl_up_sync(0xffffffffu, ip, o);
+        if (lane >= o) {
+          inc += a;
+          ia += b;
+          ip += d;
+        }
+      }
+      if (e < E) {
+        off[e] = run + inc - c;
+        cur[e] = run + inc - c;
+        if (c > 0) {
+          act[nact + ia - 1] = e;
+          cumP[nact + ia - 1] = runP + ip - pc;
+        }
+      }
+      run += __shfl_sync(0xffffffffu, inc, 31);
+      nact += __shfl_sync(0xffffffffu, ia, 31);
+      runP += __shfl_sync(0xffffffffu, ip, 31);
+    }
+    if (lane == 0) {
+      off[E] = run;
+      cumP[nact] = runP;
+      s_nact = nact;
+      s_nA = runP * (p.I / 16) * kDdSplitA;
+      s_nB = runP * (p.H / 32);
+    }
+  }
+  __syncthreads();
+  if (warp == 0) ordered_slot_scatter(eid, p.n_tok, cur, slots, lane);
+  if (p.zero_rows) {  // expert parallelism: tokens with no local slot get a zero row
+    for (int m = blockIdx.x * kDdThreads + tid; m < p.M; m += gridDim.x * kDdThreads)
+      if (tokcnt[m] == 0)
+        for (int h = 0; h < p.H; h += 8)
+          *reinterpret_cast<uint4*>(p.out + (size_t)m * p.H + h) = make_uint4(0, 0, 0, 0);
+  }
+  __syncthreads();
+
+  const int nact = s_nact, nA = s_nA, nB = s_nB;
+  const int PA = p.I / 16;             // gate/up pairs per expert pass
+  const int PB = p.H / 32;             // 32-row blocks per expert pass
+  const int nrtA = 2 * p.I / 16, nchA = p.H / 64;
+  const int nrtB = p.H / 16, nchB = p.I / 64;
+  const int nwarps = gridDim.x * kDdWarps;
+  const int gw = blockIdx.x * kDdWarps + warp;
+
+  // pass index pi (over all active experts' passes) -> active expert j
+  auto expert_of_pass = [&](int pi) {
+    int lo = 0, hi = nact - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (cumP[mid] <= pi) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+  };
+
+  for (int u = gw; u < nA + nB; u += nwarps) {
+    if (u < nA) {
+      // ======================= w13 unit: (pass, pair q, K half h) =======================
+      const int h = u % kDdSplitA, pu = u / kDdSplitA;
+      const int pi = pu / PA, q = pu - pi * PA;
+      const int j = expert_of_pass(pi);
+      const int e = act[j], pass = pi - cumP[j];
+      const int T = cnt[e], base = off[e] + pass * kDdNB;
+      const int ntok = min(kDdNB, T - pass * kDdNB);
+      const int col = g < ntok ? g : 0;  // this lane's B column (token); extra columns are ignored
+      const int slot = slots[base + col];
+      const __nv_bfloat16* xrow = p.hidden + (size_t)(slot / p.topk) * p.hidden_ld;
+      const int c0 = h * (nchA / kDdSplitA), c1 = c0 + nchA / kDdSplitA;
+      const size_t bg = ((size_t)e * nrtA + q) * nchA, bu = ((size_t)e * nrtA + PA + q) * nchA;
+      float accg[4] = {0.f, 0.f, 0.f, 0.f}, accu[4] = {0.f, 0.f, 0.f, 0.f};
+      DdChunk ring[kDdD];
+#pragma unroll
+      for (int d = 0; d < kDdD; ++d)
+        if (c0 + d < c1) dd_load_chunk(ring[d], p.w13, p.s13, bg + c0 + d, bu + c0 + d, lane, g);
+      for (int c = c0; c < c1; c += kDdD) {
+#pragma unroll
+        for (int d = 0; d < kDdD; ++d) {
+          if (c + d < c1) {
+            uint32_t b[8];
+            dd_load_b<false>(b, xrow, c + d, t);
+            dd_chunk_mma(accg, ring[d].w[0], ring[d].s[0], b);
+            dd_chunk_mma(accu, ring[d].w[1], ring[d].s[1], b);
+            if (c + d + kDdD < c1)
+              dd_load_chunk(ring[d], p.w13, p.s13, bg + c + d + kDdD, bu + c + d + kDdD, lane, g);
+          }
+        }
+      }
+      // the two K halves meet in shared memory (warps 2k, 2k+1 of this CTA)
+      float* xc = &xchg[warp >> 1][0][lane];
+      if (h == 1) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          xc[i * 32] = accg[i];
+          xc[(4 + i) * 32] = accu[i];
+        }
+      }
+      named_barrier_sync(1 + (warp >> 1), 64);
+      if (h == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          accg[i] += xc[i * 32];
+          accu[i] += xc[(4 + i) * 32];
+        }
+        // rows g, g+8 of pair q; token columns 2t, 2t+1
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int cc = 2 * t + (i & 1), row = q * 16 + g + 8 * (i >> 1);
+          if (cc < ntok)
+            p.inter[(size_t)slots[base + cc] * p.I + row] = __float2bfloat16(silu_f(accg[i]) * accu[i]);
+        }
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(p.ready + e, 1);
+      }
+      named_barrier_sync(1 + (warp >> 1), 64);  // xchg free for the next pair
+    } else {
+      // ======================= w2 unit: (pass, 32-row block rb) =======================
+      const int ub = u - nA;
+      const int pi = ub / PB, rb = ub - pi * PB;
+      const int j = expert_of_pass(pi);
+      const int e = act[j], pass = pi - cumP[j];
+      const int T = cnt[e], base = off[e] + pass * kDdNB;
+      const int ntok = min(kDdNB, T - pass * kDdNB);
+      const int col = g < ntok ? g : 0;
+      const int slot = slots[base + col];
+      const __nv_bfloat16* irow = p.inter + (size_t)slot * p.I;
+      const size_t b0 = ((size_t)e * nrtB + 2 * rb) * nchB, b1 = b0 + nchB;
+      float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+      DdChunk ring[kDdD];
+#pragma unroll
+      for (int d = 0; d < kDdD; ++d)
+        if (d < nchB) dd_load_chunk(ring[d], p.w2, p.s2, b0 + d, b1 + d, lane, g);
+      // intermediate rows of expert e are complete once all its pairs of all passes published
+      if (lane == 0) {
+        const int target = PA * ((T + kDdNB - 1) / kDdNB);
+        const long long t0 = clock64();
+        while (ld_acquire_gpu(p.ready + e) < target) {
+          if (clock64() - t0 > kDdBudget) {
+            atomicOr(p.sched + kDdSchedError, kDdErrReady);
+            break;
+          }
+          __nanosleep(64);
+        }
+      }
+      __syncwarp();
+      for (int c = 0; c < nchB; c += kDdD) {
+#pragma unroll
+        for (int d = 0; d < kDdD; ++d) {
+          if (c + d < nchB) {
+            uint32_t b[8];
+            dd_load_b<true>(b, irow, c + d, t);
+            dd_chunk_mma(acc0, ring[d].w[0], ring[d].s[0], b);
+            dd_chunk_mma(acc1, ring[d].w[1], ring[d].s[1], b);
+            if (c + d + kDdD < nchB) dd_load_chunk(ring[d], p.w2, p.s2, b0 + c + d + kDdD, b1 + c + d + kDdD, lane, g);
+          }
+        }
+      }
+      // router-weighted fp32 partials: rows rb*32 + {g, g+8} (+16), token columns 2t, 2t+1
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int cc = 2 * t + (i & 1);
+        if (cc < ntok) {
+          const int s = slots[base + cc];
+          const float wt = p.topk_w[s];
+          const int row = rb * 32 + g + 8 * (i >> 1);
+          p.partial[(size_t)s * p.H + row] = acc0[i] * wt;
+          p.partial[(size_t)s * p.H + row + 16] = acc1[i] * wt;
+        }
+      }
+      __threadfence();
+      __syncwarp();
+      // the last unit to finish (token, row block) sums the token's partials in slot order
+      int mine = -1;
+      if (lane < ntok) {
+        const int m = slots[base + lane] / p.topk;
+        int* cptr = p.counters + (size_t)m * PB + rb;
+        if (atomicAdd(cptr, 1) == tokcnt[m] - 1) {
+          *cptr = 0;  // self-cleaning
+          mine = m;
+        }
+      }
+      unsigned todo = __ballot_sync(0xffffffffu, mine >= 0);
+      if (todo) __threadfence();
+      while (todo) {
+        const int src = __ffs(todo) - 1;
+        todo &= todo - 1;
+        const int m = __shfl_sync(0xffffffffu, mine, src);
+        const int hr = rb * 32 + lane;
+        const float* pp = p.partial + (size_t)m * p.topk * p.H + hr;
+        float sum = 0.f;
+        for (int tt = 0; tt < p.topk; ++tt) {
+          const int s = m * p.topk + tt;
+          const float x = __ldcg(pp + (size_t)tt * p.H);
+          if ((sok[s >> 5] >> (s & 31)) & 1u) sum += x;
+        }
+        p.out[(size_t)m * p.H + hr] = __float2bfloat16(sum);
+      }
+    }
+  }
+
+  // ---------------- teardown: the last CTA resets the readiness counters ----------------
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    if (atomicAdd(p.sched + kDdSchedDone, 1) == (int)gridDim.x - 1) {
+      p.sched[kDdSchedDone] = 0;
+      for (int e = 0; e < E; ++e) p.ready[e] = 0;
+      __threadfence();
+    }
+  }
+}
+
+size_t decode_direct_smem_bytes(const DecodeParams& p) {
+  return (size_t)(5 * p.E + 2 + 2 * p.n_tok + p.M + p.n_tok / 32 + 1) * 4;
+}
+
+// Shapes the kernel supports: pairs split in two K halves of whole 64-k chunks.
+bool decode_direct_ok(const DecodeParams& p, int max_smem) {
+  return p.NG == 1 && (p.H / 64) % kDdSplitA == 0 && p.H % 32 == 0 && p.I % 16 == 0 &&
+         decode_direct_smem_bytes(p) + 4096 <= (size_t)max_smem;
+}
+
+cudaError_t launch_decode_direct(const DecodeParams& p, cudaStream_t stream) {
+  static thread_local size_t configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  const size_t smem = decode_direct_smem_bytes(p);
+  if (smem > 48 * 1024 && configured[dev] < smem) {
+    cudaError_t err = cudaFuncSetAttribute(moe_decode_direct_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)smem);
+    if (err != cudaSuccess) return err;
+    configured[dev] = smem;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.grid);
+  cfg.blockDim = dim3(kDdThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, moe_decode_direct_kernel, p);
+}
+
+}  // namespace w4moe

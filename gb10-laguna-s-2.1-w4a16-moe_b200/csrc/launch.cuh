@@ -93,8 +93,12 @@ struct DecodeParams {
   long long* trace;          // optional event timestamps of CTA 0 (diagnostics; nullptr normally)
   // plan (decode_plan); the stage geometry is derived per CTA on the device
   int NG, RP, R2, n_red, red_offset, ring_offset, ring_bytes, smem_bytes, grid;
+  int ring_div;              // stages are sized to ring_bytes / ring_div
 };
 int decode_plan(DecodeParams& p, int sms, int max_smem);
+// decode_direct.cu: per-warp weight streaming for <= ~1.5 slots per expert (NG == 1)
+bool decode_direct_ok(const DecodeParams& p, int max_smem);
+cudaError_t launch_decode_direct(const DecodeParams& p, cudaStream_t stream);
 
 // ---- prefill.cu (tcgen05 grouped GEMMs for large M) ----
 struct PrefillParams {
