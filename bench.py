@@ -57,13 +57,13 @@ def _peaks() -> dict:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
 
 
-def _traffic(M: int) -> float | None:
+def _traffic(M: int, key: str = "decode") -> float | None:
     """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
     p = REPO / "profiles" / "traffic.json"
     if not p.is_file():
         return None
     d = json.loads(p.read_text())
-    v = d.get(f"decode_M{M}")
+    v = d.get(f"{key}_M{M}")
     return float(v) if v is not None else None
 
 
@@ -348,7 +348,12 @@ def run_ours(args) -> int:
     # the library runs M*topk <= 4096 slots through its single fused kernel
     fused = M * TOPK <= 4096
     if fused:  # one persistent kernel does routing + w13 + w2 + top-k sum
-        kname, kbytes = "moe_decode_fused_kernel (routing + w13 + w2 + top-k sum)", wbytes
+        # same selection as the library: <= 1.5 slots per active expert, 2 <= M
+        # and the hidden rows fit shared memory -> per-warp streaming kernel
+        direct = (M * TOPK) / max(1, min(M * TOPK, E)) <= 1.5 and 2 <= M and M * H * 2 <= 72 * 1024
+        kname = ("moe_decode_direct_kernel" if direct else "moe_decode_fused_kernel") + \
+            " (routing + w13 + w2 + top-k sum)"
+        kbytes = wbytes
         achieved = kbytes / (w13_mean * 1e-3) / 1e9
         roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                     "frac": achieved / peaks["hbm_gbs"], "traffic": _traffic(M), "kernel": kname,
@@ -358,7 +363,7 @@ def run_ours(args) -> int:
         kflops = 2.0 * M * TOPK * (2 * I) * H
         achieved = kflops / (w13_mean * 1e-3) / 1e12
         roofline = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                    "frac": achieved / peaks["bf16_tflops"], "traffic": _traffic(M),
+                    "frac": achieved / peaks["bf16_tflops"], "traffic": _traffic(M, "prefill_w13"),
                     "kernel": "moe_prefill_kernel<0> (w13 + SiLU*up, tcgen05)", "kernel_us": 1e3 * w13_mean,
                     "w2_and_sum_us": 1e3 * sum(w2_ms) / len(w2_ms),
                     "peak_src": f"{peaks['src']} bf16_tflops (cuBLAS burst)",
