@@ -680,13 +680,9 @@ int decode_plan(DecodeParams& p, int sms, int max_smem) {
   if (p.ring_bytes < 3 * (minA > minB ? minA : minB)) return 0;
   p.smem_bytes = p.ring_offset + p.ring_bytes;
   p.grid = sms;
-  if (p.ring_div <= 0) {
-    static const int env_div = [] {
-      const char* e = getenv("W4A16_DECODE_RING_DIV");
-      return e ? atoi(e) : 0;
-    }();
-    p.ring_div = env_div > 0 ? env_div : 3;
-  }
+  // three large stages: measured best (more, smaller stages cost more
+  // per-stage handshakes than they hide latency)
+  if (p.ring_div <= 0) p.ring_div = 3;
   return 1;
 }
 
