@@ -321,6 +321,11 @@ int w4a16_moe_forward(const void* hidden, int64_t M, int64_t H, int64_t hidden_l
       mark_stage(0, st);
       mark_stage(1, st);
       static const bool staged_only = getenv("W4A16_DECODE_STAGED") != nullptr;  // A/B comparisons
+      static const int direct_min_m = [] {
+        const char* e = getenv("W4A16_DECODE_DIRECT_MIN_M");
+        return e ? atoi(e) : 2;
+      }();
+      dp.direct_min_m = direct_min_m;
       cudaError_t err = (!staged_only && decode_direct_ok(dp, max_smem_optin() - 1024)) ? launch_decode_direct(dp, st)
                                                                                          : launch_decode(dp, st);
       if (err != cudaSuccess) return cuda_fail(err, "w4a16_moe_forward/decode");

@@ -274,7 +274,32 @@ __global__ void __launch_bounds__(kDdThreads, 1) moe_decode_direct_kernel(Decode
     return lo;
   };
 
+  // w2 unit ub -> first fragment block of its row tile
+  auto w2_block = [&](int ub) {
+    const int half = ub & 1;
+    const int pi = (ub >> 1) / PB, rb = (ub >> 1) - pi * PB;
+    const int e = act[expert_of_pass(pi)];
+    return ((size_t)e * nrtB + 2 * rb + half) * nchB;
+  };
+  auto issue_w2 = [&](int ub) {  // whole row tile -> this warp's buffer (lane 0)
+    const size_t b0 = w2_block(ub);
+    mbar_arrive_expect_tx(&wbar[warp], (uint32_t)nchB * 576);
+    bulk_g2s(wbuf, p.w2 + b0 * 512, (uint32_t)nchB * 512, &wbar[warp]);
+    bulk_g2s(wbuf + nchB * 512, p.s2 + b0 * 64, (uint32_t)nchB * 64, &wbar[warp]);
+  };
   uint32_t wphase = 0;  // w2 tiles this warp has loaded (its barrier's parity)
+  // The first w2 unit of this warp (often a second-round unit after a w13
+  // unit) is copied at kernel start, so all first-round w2 weights stream
+  // concurrently with the w13 units.
+  int prefetched = -1;
+  {
+    int u0 = gw;
+    if (u0 < nA) u0 += ((nA - u0 + nwarps - 1) / nwarps) * nwarps;
+    if (u0 < nA + nB) {
+      prefetched = u0;
+      if (lane == 0) issue_w2(u0 - nA);
+    }
+  }
   for (int u = gw; u < nA + nB; u += nwarps) {
     const bool first = u == gw;
     if (first) dd_trace(tr, warp, 0);
@@ -339,11 +364,7 @@ __global__ void __launch_bounds__(kDdThreads, 1) moe_decode_direct_kernel(Decode
       // the whole row tile (nchB x 512 B words + nchB x 64 B scales, each
       // contiguous) is bulk-copied into this warp's buffer before the
       // readiness wait, so w2 weights stream while the w13 units still run
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&wbar[warp], (uint32_t)nchB * 576);
-        bulk_g2s(wbuf, p.w2 + b0 * 512, (uint32_t)nchB * 512, &wbar[warp]);
-        bulk_g2s(wbuf + nchB * 512, p.s2 + b0 * 64, (uint32_t)nchB * 64, &wbar[warp]);
-      }
+      if (lane == 0 && u != prefetched) issue_w2(ub);
       // intermediate rows of expert e are complete once all its pairs of all passes published
       if (lane == 0) {
         const int target = PA * ((T + kDdNB - 1) / kDdNB);
@@ -448,9 +469,7 @@ size_t decode_direct_smem_bytes(const DecodeParams& p) {
 
 // Shapes the kernel supports: pairs split in two K halves of whole 64-k chunks.
 bool decode_direct_ok(const DecodeParams& p, int max_smem) {
-  // M = 1 stays on the staged kernel: one token's 10 experts are too few
-  // weight streams for per-warp loads to beat its bulk copies
-  return p.NG == 1 && p.M >= 2 && (p.H / 64) % kDdSplitA == 0 && p.H % 32 == 0 && p.I % 16 == 0 && p.I / 64 <= kDdMaxChB &&
+  return p.NG == 1 && p.M >= p.direct_min_m && (p.H / 64) % kDdSplitA == 0 && p.H % 32 == 0 && p.I % 16 == 0 && p.I / 64 <= kDdMaxChB &&
          (((uintptr_t)p.w2 | (uintptr_t)p.s2) & 15) == 0 &&
          (size_t)p.M * p.H * 2 <= (size_t)kDdMaxXBytes &&
          decode_direct_smem_bytes(p) + sizeof(float) * 8 * 8 * 32 + 1024 <= (size_t)max_smem;

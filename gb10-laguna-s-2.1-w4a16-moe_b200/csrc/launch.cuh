@@ -94,6 +94,7 @@ struct DecodeParams {
   // plan (decode_plan); the stage geometry is derived per CTA on the device
   int NG, RP, R2, n_red, red_offset, ring_offset, ring_bytes, smem_bytes, grid;
   int ring_div;              // stages are sized to ring_bytes / ring_div
+  int direct_min_m;          // smallest M sent to the direct-streaming kernel
 };
 int decode_plan(DecodeParams& p, int sms, int max_smem);
 // decode_direct.cu: per-warp weight streaming for <= ~1.5 slots per expert (NG == 1)
