@@ -103,12 +103,12 @@ struct ItemView {
   int base;  // start of e's slots in the per-CTA slot list
 };
 
-__device__ __forceinline__ int stage_bytes_for(int R, int nc, int rows) {
+__host__ __device__ __forceinline__ int stage_bytes_for(int R, int nc, int rows) {
   return R * nc * 576 + rows * (nc * 128 + 16);
 }
 
 // Largest divisor nc of nchunks with stage bytes <= cap (0 if none).
-__device__ __forceinline__ int pick_nc(int nchunks, int R, int rows, int cap) {
+__host__ __device__ __forceinline__ int pick_nc(int nchunks, int R, int rows, int cap) {
   int best = 0;
   for (int nc = 1; nc <= nchunks; ++nc)
     if (nchunks % nc == 0 && stage_bytes_for(R, nc, rows) <= cap) best = nc;
@@ -200,14 +200,15 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
       off[E] = run;
       s_nact = nact;
       // stage geometry: the largest stages that still fit three in the ring
+      // stage geometry for this many reserved activation rows, precomputed
+      // on the host (decode_plan) for every row count 1..NB
+      const int rr = max(1, min(NB, mx));
       Geometry gm;
-      gm.rows_res = max(1, min(NB, mx));
-      const int cap = p.ring_bytes / p.ring_div / 128 * 128;
-      gm.ncA = pick_nc(p.H / 64, 2 * p.RP, gm.rows_res, cap);
-      gm.ncB = pick_nc(p.I / 64, p.R2, gm.rows_res, cap);
-      gm.stage_bytes = (max(stage_bytes_for(2 * p.RP, gm.ncA, gm.rows_res),
-                            stage_bytes_for(p.R2, gm.ncB, gm.rows_res)) + 127) / 128 * 128;
-      gm.n_stages = min(kDecMaxStages, p.ring_bytes / gm.stage_bytes);
+      gm.rows_res = rr;
+      gm.ncA = p.geo[rr][0];
+      gm.ncB = p.geo[rr][1];
+      gm.stage_bytes = p.geo[rr][2];
+      gm.n_stages = p.geo[rr][3];
       s_geo = gm;
     }
   }
@@ -683,6 +684,20 @@ int decode_plan(DecodeParams& p, int sms, int max_smem) {
   // three large stages: measured best (more, smaller stages cost more
   // per-stage handshakes than they hide latency)
   if (p.ring_div <= 0) p.ring_div = 3;
+  // stage geometry per reserved row count: the largest stages that still fit
+  // ring_div of them in the ring
+  const int cap = p.ring_bytes / p.ring_div / 128 * 128;
+  for (int rr = 1; rr <= 8 * NG && rr < kDecGeoRows; ++rr) {
+    const int ncA = pick_nc(p.H / 64, 2 * RP, rr, cap), ncB = pick_nc(p.I / 64, R2, rr, cap);
+    if (ncA == 0 || ncB == 0) return 0;
+    const int sb = ((stage_bytes_for(2 * RP, ncA, rr) > stage_bytes_for(R2, ncB, rr) ? stage_bytes_for(2 * RP, ncA, rr)
+                                                                                       : stage_bytes_for(R2, ncB, rr)) +
+                    127) / 128 * 128;
+    p.geo[rr][0] = ncA;
+    p.geo[rr][1] = ncB;
+    p.geo[rr][2] = sb;
+    p.geo[rr][3] = p.ring_bytes / sb < kDecMaxStages ? p.ring_bytes / sb : kDecMaxStages;
+  }
   return 1;
 }
 

@@ -71,6 +71,7 @@ int gemv_blocks_per_sm(int mode, int ng);
 
 // ---- decode.cu (fused persistent small-M layer) ----
 constexpr int kDecodeMaxSlots = 4096;  // M*topk handled by the fused kernel
+constexpr int kDecGeoRows = 33;        // stage geometry table rows (reserved activation rows 1..32)
 
 struct DecodeParams {
   const uint8_t* w13;        // fragment-major w13 (gate rows [0,I), up rows [I,2I))
@@ -95,6 +96,7 @@ struct DecodeParams {
   int NG, RP, R2, n_red, red_offset, ring_offset, ring_bytes, smem_bytes, grid;
   int ring_div;              // stages are sized to ring_bytes / ring_div
   int direct_min_m;          // smallest M sent to the direct-streaming kernel
+  int geo[kDecGeoRows][4];   // per reserved row count: ncA, ncB, stage bytes, stages
 };
 int decode_plan(DecodeParams& p, int sms, int max_smem);
 // decode_direct.cu: per-warp weight streaming for <= ~1.5 slots per expert (NG == 1)
