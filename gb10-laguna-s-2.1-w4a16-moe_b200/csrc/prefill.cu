@@ -369,13 +369,44 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   } else {
     // ======================= epilogue warps =======================
     const int r = warp * 32 + lane;  // TMEM lane = weight row within the item
+    constexpr int kGroups = kPfMaxTok / 32;
     for (int n = 0; n < my_items; ++n) {
       const PfItem it = item_of(n);
       const int b = n & 1;
+      // w2: slots and router weights of the item's columns, loaded while the
+      // MMAs still run (one dependent round trip per item, not per column group)
+      int sl_r[kGroups];
+      float w_r[kGroups];
+      if (MODE == 1) {
+#pragma unroll
+        for (int k = 0; k < kGroups; ++k) {
+          const int cl = k * 32 + lane;
+          sl_r[k] = cl < it.ntok ? p.sorted[it.base + cl] : 0;
+        }
+#pragma unroll
+        for (int k = 0; k < kGroups; ++k) w_r[k] = k * 32 + lane < it.ntok ? p.topk_w[sl_r[k]] : 0.f;
+      }
       wait(&acc_full[b], (n >> 1) & 1);
       tc_fence_after();
       const uint32_t dbase = tmem + (uint32_t)(b * 256) + ((uint32_t)(warp * 32) << 16);
-      for (int c0 = 0; c0 < it.n16; c0 += 32) {
+      if (MODE == 1) {
+#pragma unroll
+        for (int k = 0; k < kGroups; ++k) {
+          const int c0 = k * 32;
+          if (c0 >= it.n16) break;
+          uint32_t v[32];
+          tmem_ld32(dbase + c0, v);
+          const int ncol = min(32, it.ntok - c0);
+          __nv_bfloat16* dst = p.partial + it.p * 128 + r;
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const int slot = __shfl_sync(0xffffffffu, sl_r[k], c);
+            const float wt = __shfl_sync(0xffffffffu, w_r[k], c);
+            if (c < ncol) dst[(size_t)slot * p.H] = __float2bfloat16(__uint_as_float(v[c]) * wt);
+          }
+        }
+      }
+      for (int c0 = 0; MODE == 0 && c0 < it.n16; c0 += 32) {
         uint32_t v[32];
         tmem_ld32(dbase + c0, v);
         if (MODE == 0) {
@@ -398,19 +429,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
               }
             }
             named_barrier_sync(2, kPfEpiWarps * 32);
-          }
-        } else {
-          // slot and router weight of column c0 + lane, broadcast per column
-          const int cl = c0 + lane;
-          const int my_slot = cl < it.ntok ? p.sorted[it.base + cl] : 0;
-          const float my_w = cl < it.ntok ? p.topk_w[my_slot] : 0.f;
-          const int ncol = min(32, it.ntok - c0);
-#pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const int slot = __shfl_sync(0xffffffffu, my_slot, c);
-            const float wt = __shfl_sync(0xffffffffu, my_w, c);
-            if (c < ncol)
-              p.partial[(size_t)slot * p.H + it.p * 128 + r] = __float2bfloat16(__uint_as_float(v[c]) * wt);
           }
         }
       }
