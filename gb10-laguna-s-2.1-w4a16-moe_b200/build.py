@@ -66,13 +66,18 @@ def _needs_build(sources: list[Path], headers: list[Path], out: Path, stamp: Pat
     return any(p.stat().st_mtime > t for p in sources + headers)
 
 
-def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -> Path:
+def build(force: bool = False, jobs: int | None = None, verbose: bool = False, diagnostics: bool = False) -> Path:
+    """Compile the library.  ``diagnostics`` adds -DW4A16_DIAGNOSTICS: the
+    forward then honours the W4A16_*_TRACE / W4A16_DECODE_* environment hooks
+    (pipeline timestamps, kernel selection overrides) -- for profiling builds,
+    never for production."""
     nvcc = nvcc_path()
     sources = sorted(CSRC.glob("*.cu"))
     headers = sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
     out = lib_path()
     stamp = BUILD_DIR / "flags.sha1"
-    digest = _flags_digest([])
+    extra = ["-DW4A16_DIAGNOSTICS"] if diagnostics else []
+    digest = _flags_digest(extra)
     if not force and not _needs_build(sources, headers, out, stamp, digest):
         return out
     BUILD_DIR.mkdir(parents=True, exist_ok=True)
@@ -80,7 +85,7 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -
 
     def compile_one(src: Path) -> Path:
         obj = BUILD_DIR / (src.stem + ".o")
-        cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, f"-I{INCLUDE}", "-c", str(src), "-o", str(obj)]
+        cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, *extra, f"-I{INCLUDE}", "-c", str(src), "-o", str(obj)]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
         res = subprocess.run(cmd, capture_output=True, text=True)
@@ -107,8 +112,9 @@ def main(argv: list[str] | None = None) -> int:
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--jobs", type=int, default=None)
     ap.add_argument("--verbose", action="store_true", help="print ptxas register/spill info")
+    ap.add_argument("--diagnostics", action="store_true", help="enable the environment trace / override hooks")
     args = ap.parse_args(argv)
-    print(build(force=args.force, jobs=args.jobs, verbose=args.verbose))
+    print(build(force=args.force, jobs=args.jobs, verbose=args.verbose, diagnostics=args.diagnostics))
     return 0
 
 

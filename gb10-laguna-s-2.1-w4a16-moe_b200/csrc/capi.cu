@@ -316,15 +316,22 @@ int w4a16_moe_forward(const void* hidden, int64_t M, int64_t H, int64_t hidden_l
     dp.ready = ws.ready;
     dp.sched = ws.sched;
     dp.zero_rows = expert_map != nullptr;
+#ifdef W4A16_DIAGNOSTICS
     if (const char* tr = getenv("W4A16_DECODE_TRACE")) dp.trace = (long long*)strtoull(tr, nullptr, 0);
+#endif
     if (decode_plan(dp, sm_count(), max_smem_optin() - 1024)) {
       mark_stage(0, st);
       mark_stage(1, st);
+#ifdef W4A16_DIAGNOSTICS
       static const bool staged_only = getenv("W4A16_DECODE_STAGED") != nullptr;  // A/B comparisons
       static const int direct_min_m = [] {
         const char* e = getenv("W4A16_DECODE_DIRECT_MIN_M");
         return e ? atoi(e) : 2;
       }();
+#else
+      constexpr bool staged_only = false;
+      constexpr int direct_min_m = 2;  // M = 1 measured faster on the staged kernel
+#endif
       dp.direct_min_m = direct_min_m;
       cudaError_t err = (!staged_only && decode_direct_ok(dp, max_smem_optin() - 1024)) ? launch_decode_direct(dp, st)
                                                                                          : launch_decode(dp, st);
@@ -398,7 +405,9 @@ int w4a16_moe_forward(const void* hidden, int64_t M, int64_t H, int64_t hidden_l
     p13.topk_w = topk_weights;
     p13.sched = ws.sched;
     p13.n_stages = prefill_stages((int)E, max_smem_optin());
+#ifdef W4A16_DIAGNOSTICS
     if (const char* tr = getenv("W4A16_PREFILL_TRACE")) p13.trace = (long long*)strtoull(tr, nullptr, 0);
+#endif
     PrefillParams p2 = p13;
     if (getenv("W4A16_PREFILL_TRACE_W2") == nullptr) p2.trace = nullptr;
     else p13.trace = nullptr;
