@@ -348,11 +348,7 @@ def run_ours(args) -> int:
     # the library runs M*topk <= 4096 slots through its single fused kernel
     fused = M * TOPK <= 4096
     if fused:  # one persistent kernel does routing + w13 + w2 + top-k sum
-        # same selection as the library: <= 1.5 slots per active expert, 2 <= M
-        # and the hidden rows fit shared memory -> per-warp streaming kernel
-        direct = (M * TOPK) / max(1, min(M * TOPK, E)) <= 1.5 and 2 <= M and M * H * 2 <= 72 * 1024
-        kname = ("moe_decode_direct_kernel" if direct else "moe_decode_fused_kernel") + \
-            " (routing + w13 + w2 + top-k sum)"
+        kname = "moe_decode_fused_kernel (routing + w13 + w2 + top-k sum)"
         kbytes = wbytes
         achieved = kbytes / (w13_mean * 1e-3) / 1e9
         roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",

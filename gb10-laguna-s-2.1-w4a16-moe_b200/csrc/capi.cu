@@ -144,8 +144,9 @@ int w4a16_version(void) { return 100; }
 
 int w4a16_set_path(int path) {
   g_last_error.clear();
-  if (path < 0 || path > 2)
-    return fail(kInvalidArgument, "w4a16_set_path: 0 = auto, 1 = general, 2 = tensor-core prefill");
+  if (path < 0 || path > 3)
+    return fail(kInvalidArgument,
+                "w4a16_set_path: 0 = auto, 1 = general, 2 = tensor-core prefill, 3 = direct-streaming decode");
   g_force_general = path;
   return kOk;
 }
@@ -293,7 +294,7 @@ int w4a16_moe_forward(const void* hidden, int64_t M, int64_t H, int64_t hidden_l
                     (int)(expert_map ? global_num_experts : E), (int)E};
 
   // Small M: one fused persistent kernel (routing + w13 + w2 + top-k sum).
-  if (!g_force_general && ((uintptr_t)hidden & 15) == 0 && (hidden_ld & 7) == 0) {
+  if ((g_force_general == 0 || g_force_general == 3) && ((uintptr_t)hidden & 15) == 0 && (hidden_ld & 7) == 0) {
     DecodeParams dp{};
     dp.w13 = (const uint8_t*)w13_rep;
     dp.s13 = (const uint8_t*)s13_rep;
@@ -330,9 +331,11 @@ int w4a16_moe_forward(const void* hidden, int64_t M, int64_t H, int64_t hidden_l
       }();
 #else
       constexpr bool staged_only = false;
-      constexpr int direct_min_m = 2;  // M = 1 measured faster on the staged kernel
+      // the staged kernel measured at least as fast at every M (B200,
+      // E=256 top-10 3072x1024), so the direct kernel runs only on request
+      constexpr int direct_min_m = 1 << 30;
 #endif
-      dp.direct_min_m = direct_min_m;
+      dp.direct_min_m = g_force_general == 3 ? 1 : direct_min_m;
       cudaError_t err = (!staged_only && decode_direct_ok(dp, max_smem_optin() - 1024)) ? launch_decode_direct(dp, st)
                                                                                          : launch_decode(dp, st);
       if (err != cudaSuccess) return cuda_fail(err, "w4a16_moe_forward/decode");

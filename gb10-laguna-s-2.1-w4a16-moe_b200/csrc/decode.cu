@@ -657,8 +657,21 @@ int decode_plan(DecodeParams& p, int sms, int max_smem) {
   const double avg = (double)n_tok / (double)(max_active > 0 ? max_active : 1);
   const int NG = avg <= 1.5 ? 1 : (avg <= 6.0 ? 2 : 4);
   const int M = p.M;
-  int RP = M <= 16 ? 1 : (M <= 64 ? 2 : 4);
-  int R2 = M <= 16 ? 2 : (M <= 64 ? 4 : 8);
+  // item sizes (row tiles per w13 / w2 item), measured on B200 at E=256
+  // top-10 3072x1024: larger items amortise per-item handoffs until too few
+  // items remain to balance over the SMs
+  int RP = M <= 16 ? 2 : 4;
+  int R2 = M <= 16 ? 4 : 8;
+#ifdef W4A16_DIAGNOSTICS
+  if (M > 64) {
+    if (const char* e = getenv("W4A16_DECODE_RP_LARGE")) RP = atoi(e);
+    if (const char* e = getenv("W4A16_DECODE_R2_LARGE")) R2 = atoi(e);
+  }
+#endif
+#ifdef W4A16_DIAGNOSTICS
+  if (const char* e = getenv("W4A16_DECODE_RP")) RP = atoi(e);
+  if (const char* e = getenv("W4A16_DECODE_R2")) R2 = atoi(e);
+#endif
   while (RP > 1 && (p.I / 16) % RP) RP >>= 1;
   while (R2 > 2 && (p.H / 16) % R2) R2 >>= 1;
   if ((p.H / 16) % R2 || (p.I / 16) % RP) return 0;

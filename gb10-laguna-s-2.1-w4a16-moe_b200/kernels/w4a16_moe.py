@@ -324,9 +324,11 @@ def set_stage_events(events: list | None) -> None:
 def set_path(path: str) -> None:
     """Select the forward implementation for the calling thread: ``"auto"``
     (fused persistent kernel for small M, tensor-core kernels otherwise),
-    ``"general"`` (multi-kernel CUDA-core path) or ``"prefill"`` (the
-    tensor-core path at any M)."""
-    _check(load_library().w4a16_set_path({"auto": 0, "general": 1, "prefill": 2}[path]), "w4a16_set_path")
+    ``"general"`` (multi-kernel CUDA-core path), ``"prefill"`` (the
+    tensor-core path at any M) or ``"direct"`` (the direct-streaming decode
+    kernel wherever it applies, the staged one otherwise)."""
+    _check(load_library().w4a16_set_path({"auto": 0, "general": 1, "prefill": 2, "direct": 3}[path]),
+           "w4a16_set_path")
 
 
 def read_status(hidden_shape: tuple[int, int], topk: int, num_experts: int, intermediate: int,

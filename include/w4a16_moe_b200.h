@@ -48,9 +48,11 @@ W4A16_API int w4a16_set_stage_events(void* const* events, int n_events);
 
 /*
  * Path selection for the calling thread (no reference counterpart; used by
- * tests to cover both implementations): 0 = automatic (fused persistent
- * kernel for small M, multi-kernel path otherwise), 1 = always the
- * multi-kernel path.
+ * tests to cover every implementation): 0 = automatic (staged fused
+ * persistent kernel for M*topk <= 4096, tcgen05 prefill kernels or the
+ * CUDA-core general path otherwise), 1 = always the general path, 2 = the
+ * tcgen05 prefill kernels wherever their shape rules allow, 3 = the
+ * direct-streaming decode kernel wherever it applies.
  */
 W4A16_API int w4a16_set_path(int path);
 
