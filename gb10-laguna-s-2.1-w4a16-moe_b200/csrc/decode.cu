@@ -694,9 +694,12 @@ int decode_plan(DecodeParams& p, int sms, int max_smem) {
   if (p.ring_bytes < 3 * (minA > minB ? minA : minB)) return 0;
   p.smem_bytes = p.ring_offset + p.ring_bytes;
   p.grid = sms;
-  // three large stages: measured best (more, smaller stages cost more
-  // per-stage handshakes than they hide latency)
-  if (p.ring_div <= 0) p.ring_div = 3;
+  // two large stages: measured best at every M (more, smaller stages cost
+  // more per-stage handshakes than they hide latency)
+  if (p.ring_div <= 0) p.ring_div = 2;
+#ifdef W4A16_DIAGNOSTICS
+  if (const char* e = getenv("W4A16_DECODE_RING_DIV")) p.ring_div = atoi(e) > 0 ? atoi(e) : p.ring_div;
+#endif
   // stage geometry per reserved row count: the largest stages that still fit
   // ring_div of them in the ring
   const int cap = p.ring_bytes / p.ring_div / 128 * 128;
