@@ -97,3 +97,35 @@ def test_library_has_no_cpu_compute_symbols(lib):
     """The library is device code + C ABI only: no host-side compute fallback."""
     out = ctypes.CDLL(str(REPO / "gb10-laguna-s-2.1-w4a16-moe_b200" / "lib" / "libw4a16moe_b200.so"))
     assert not hasattr(out, "w4a16_moe_forward_cpu")
+
+
+def test_set_path_range(lib):
+    for p in (0, 1, 2, 3):
+        assert lib.w4a16_set_path(p) == 0
+    assert lib.w4a16_set_path(4) == 1 and b"direct" in lib.w4a16_last_error()
+    assert lib.w4a16_set_path(0) == 0
+
+
+def test_align_scratch_bytes(lib):
+    lib.w4a16_moe_align_scratch_bytes.restype = ctypes.c_int64
+    lib.w4a16_moe_align_scratch_bytes.argtypes = [ctypes.c_int64, ctypes.c_int64]
+    assert lib.w4a16_moe_align_scratch_bytes(-1, 256) == -1
+    assert lib.w4a16_moe_align_scratch_bytes(100, 2000) == -1
+    assert lib.w4a16_moe_align_scratch_bytes(100, 256) == 0  # small inputs: one-CTA kernel, no scratch
+
+
+def test_ep_entry_points_reject_bad_args(lib):
+    vp, i64, c_int = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+    lib.w4a16_ep_plan.argtypes = [vp, c_int, i64, i64, i64, i64, vp, vp, vp, vp, vp]
+    lib.w4a16_ep_pack.argtypes = [vp, i64, vp, c_int, vp, i64, i64, i64, i64, vp, vp, vp, vp, vp]
+    lib.w4a16_ep_combine.argtypes = [vp, vp, i64, i64, i64, vp, vp]
+    # experts must divide evenly over the ranks
+    assert lib.w4a16_ep_plan(1, 0, 4, 2, 10, 4, 1, 1, 1, 1, None) == 1
+    assert b"divide" in lib.w4a16_last_error()
+    assert lib.w4a16_ep_plan(None, 0, 4, 2, 8, 4, 1, 1, 1, 1, None) == 1  # null ids
+    assert b"null" in lib.w4a16_last_error()
+    # H must be a multiple of 8; M == 0 is a no-op
+    assert lib.w4a16_ep_pack(1, 12, 1, 0, 1, 4, 2, 12, 2, 1, 1, 1, 1, None) == 1
+    assert lib.w4a16_ep_pack(None, 256, None, 0, None, 0, 2, 256, 2, None, None, None, None, None) == 0
+    assert lib.w4a16_ep_combine(1, 1, 4, 2, 12, 1, None) == 1
+    assert lib.w4a16_ep_combine(None, None, 0, 2, 256, None, None) == 0
