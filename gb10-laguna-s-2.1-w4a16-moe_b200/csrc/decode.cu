@@ -663,10 +663,8 @@ int decode_plan(DecodeParams& p, int sms, int max_smem) {
   int RP = M <= 16 ? 2 : 4;
   int R2 = M <= 16 ? 4 : 8;
 #ifdef W4A16_DIAGNOSTICS
-  if (M > 64) {
-    if (const char* e = getenv("W4A16_DECODE_RP_LARGE")) RP = atoi(e);
-    if (const char* e = getenv("W4A16_DECODE_R2_LARGE")) R2 = atoi(e);
-  }
+  if (const char* e = getenv("W4A16_DECODE_RP")) RP = atoi(e);
+  if (const char* e = getenv("W4A16_DECODE_R2")) R2 = atoi(e);
 #endif
 #ifdef W4A16_DIAGNOSTICS
   if (const char* e = getenv("W4A16_DECODE_RP")) RP = atoi(e);

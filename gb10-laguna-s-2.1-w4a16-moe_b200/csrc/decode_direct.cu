@@ -1,32 +1,35 @@
 // Fused small-M MoE layer for the fewest-tokens-per-expert regime (at most
-// ~1.5 routed slots per active expert, e.g. M = 1 .. ~20 at top-10 of 256):
-// routing + w13 (+SiLU*up) + w2 (+ router-weighted top-k sum) in one
-// persistent cooperative kernel in which every warp streams its own weights.
+// ~1.5 routed slots per active expert, hidden rows <= 72 KB): routing + w13
+// (+SiLU*up) + w2 (+ router-weighted top-k sum) in one persistent cooperative
+// kernel in which every warp streams its own weights.  An alternative to the
+// staged decode kernel (decode.cu), selected with w4a16_set_path(3); on B200
+// the re-tuned staged kernel measured at least as fast at every M, so the
+// automatic path does not pick this one.
 //
 // Replaces, in that regime, the reference's moe_align_block_size +
 // _w4a16_moe_w1_fused_kernel + _w4a16_moe_w2_kernel + _moe_sum_kernel
 // (kernels/w4a16_moe.py:187-290, :374-670).
 //
-// Why a second decode kernel: with one or two tokens per expert the layer is a
-// pure weight stream (53 MB at M = 1) and the staged design (a producer warp
-// filling a shared-memory ring for 16 consumer warps, per-item reductions by
-// epilogue warps) spends its time in per-stage handshakes.  Here there is no
-// producer, ring or epilogue warp:
-//   * units: w13 (expert, pass of <= 8 tokens, gate/up row-tile pair, K half)
-//            and w2 (expert, pass, 32-row block); all w13 units precede all
-//            w2 units; warp g of the grid takes units g, g + warps, ...
-//   * a warp loads its unit's fragment-major weight and scale blocks straight
-//     from global memory into registers, 2 x kDdG chunks (64 k each) ahead, decodes
-//     int4 -> bf16 (code - 8, exact) into m16n8k16 A fragments and multiplies
-//     with the tokens' activations (B fragments loaded from global / L1); the
-//     bf16 group scales multiply the fp32 partial of each 32-wide group;
-//   * w13: the two K halves of a pair run on adjacent warps of one CTA and meet
-//     in shared memory; the first writes bf16(silu(gate) * up) and bumps the
-//     expert's readiness counter;
-//   * w2: a unit bulk-copies its whole row tile into the warp's shared buffer,
-//     waits (bounded) until the expert's w13 pairs have all published, multiplies by the router weight
-//     into fp32 partials, and the last unit to finish a (token, row block)
-//     sums that token's partials in slot order (deterministic).
+// Structure (no producer warp, no stage ring, no epilogue warps):
+//   * the CTA copies the hidden rows [M, H] into shared memory once;
+//   * units: w13 (expert, pass of <= 8 tokens, gate/up pair, gate or up half)
+//            and w2 (expert, pass, 16-row tile); all w13 units precede all w2
+//            units; warp g of the grid takes units g, g + warps, ...;
+//   * a w13 warp streams its row tile's fragment-major weight and scale
+//     blocks from global memory into registers, 2 x kDdG chunks (64 k each)
+//     ahead and refilled kDdG consecutive chunks at a time (DRAM page
+//     locality), decodes int4 -> bf16 (code - 8, exact) into m16n8k16 A
+//     fragments and multiplies with B fragments read from the staged hidden
+//     rows; the bf16 group scales multiply the fp32 partial of each 32-wide
+//     group; the gate and up warps of a pair meet in shared memory, the gate
+//     warp writes bf16(silu(gate) * up) and bumps the expert's readiness
+//     counter;
+//   * a w2 warp bulk-copies its whole row tile into its shared buffer (the
+//     first one at kernel start, so w2 weights stream during the w13 units),
+//     waits (bounded) until the expert's w13 pairs have all published, copies
+//     the tokens' intermediate rows next to it, multiplies, scales by the
+//     router weight into fp32 partials, and the last unit to finish a (token,
+//     32-row block) sums that token's partials in slot order (deterministic).
 // Every wait is bounded; counters are self-cleaning.
 #include "launch.cuh"
 
