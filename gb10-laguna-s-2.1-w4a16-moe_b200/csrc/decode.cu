@@ -575,11 +575,16 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
               for (int hr = lane; hr < span; hr += 32) {
                 const float* pp = p.partial + (size_t)m * p.topk * p.H + v.q * span + hr;
                 float sum = 0.f;
-#pragma unroll 4
-                for (int tt = 0; tt < p.topk; ++tt) {
-                  const int slot = m * p.topk + tt;
-                  const float x = __ldcg(pp + (size_t)tt * p.H);
-                  if ((sok[slot >> 5] >> (slot & 31)) & 1u) sum += x;
+                for (int t0 = 0; t0 < p.topk; t0 += 16) {
+                  // all loads of a batch in flight before the ordered sum
+                  float xs[16];
+#pragma unroll
+                  for (int i = 0; i < 16; ++i) xs[i] = t0 + i < p.topk ? __ldcg(pp + (size_t)(t0 + i) * p.H) : 0.f;
+#pragma unroll
+                  for (int i = 0; i < 16; ++i) {
+                    const int slot = m * p.topk + t0 + i;
+                    if (t0 + i < p.topk && ((sok[slot >> 5] >> (slot & 31)) & 1u)) sum += xs[i];
+                  }
                 }
                 p.out[(size_t)m * p.H + v.q * span + hr] = __float2bfloat16(sum);
               }
@@ -678,7 +683,12 @@ int decode_plan(DecodeParams& p, int sms, int max_smem) {
   p.NG = NG;
   p.RP = RP;
   p.R2 = R2;
-  p.tail_reduce = M > 8;
+  // grid-wide top-k sum after all w2 items (measured faster than the
+  // per-(token, row block) last-arriver sum at every M on B200)
+  p.tail_reduce = 1;
+#ifdef W4A16_DIAGNOSTICS
+  if (const char* e = getenv("W4A16_DECODE_TAIL")) p.tail_reduce = atoi(e);
+#endif
   const int route_bytes = (4 * p.E + 1 + 2 * n_tok + M + n_tok / 32 + 1) * 4;
   p.red_offset = (route_bytes + 127) / 128 * 128;
   const int red_buf = kDecConsumers * RW * NG * 128 * 4;
