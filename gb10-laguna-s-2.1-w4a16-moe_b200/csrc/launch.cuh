@@ -103,6 +103,39 @@ int decode_plan(DecodeParams& p, int sms, int max_smem);
 bool decode_direct_ok(const DecodeParams& p, int max_smem);
 cudaError_t launch_decode_direct(const DecodeParams& p, cudaStream_t stream);
 
+// ---- decode_sliced.cu (expert-sliced fused layer, M <= 4) ----
+constexpr int kSlicedMaxM = 4;
+constexpr int kSlicedMaxSlots = 64;    // M * topk
+constexpr int kSlicedMaxPieces = 8;    // fp32 row-tile pieces one CTA may add
+constexpr int kSlicedMaxGrid = 1024;   // CTAs (piece flags in the workspace)
+
+struct SlicedParams {
+  const uint8_t *w13, *s13, *w2, *s2;  // fragment-major weights and scales
+  const __nv_bfloat16* hidden;
+  long long hidden_ld;
+  SlotMap map;
+  int n_tok, topk, M, E, H, I;
+  const float* topk_w;       // [n_tok]
+  __nv_bfloat16* out;        // [M, H]
+  __nv_bfloat16* inter;      // [n_tok, I] intermediate rows, expert-sorted, lane-permuted
+  int32_t* ready;            // [E] published w13 pairs per expert (zero between calls)
+  int32_t* readers;          // [E] CTAs done polling ready[e] (zero between calls)
+  int32_t* pflag;            // [grid] row-tile piece published (zero between calls)
+  float* pieces;             // [grid, M, 16] fp32 row-tile pieces
+  int32_t* sched;            // status word at [2]
+  long long* trace;          // optional pipeline timestamps of CTA trace_cta (diagnostics)
+  int trace_cta;
+  int diag;                  // diagnostics: bit 0 = skip the math (pipeline only)
+  int wait_ns;               // > 0: consumers back off with nanosleep between barrier checks
+  // plan (sliced_plan)
+  int grid, smem_bytes, Mp, T2, maxT, lag, nr_cap;
+  int off_x, off_inter, off_red, off_oacc, off_pc, off_table, off_rounds, off_ring, ring_bytes;
+  int n_slots, slot_bytes, max_stages, max_rounds;
+};
+int sliced_plan(SlicedParams& p, int sms, int max_smem);
+cudaError_t launch_sliced(const SlicedParams& p, cudaStream_t stream);
+__host__ __device__ long long sliced_w2_start(int c, int A, int P, int G, int chA, int chB, int nrt2);
+
 // ---- prefill.cu (tcgen05 grouped GEMMs for large M) ----
 struct PrefillParams {
   const uint8_t* w;          // fragment-major weights of this projection

@@ -325,10 +325,12 @@ def set_path(path: str) -> None:
     """Select the forward implementation for the calling thread: ``"auto"``
     (fused persistent kernel for small M, tensor-core kernels otherwise),
     ``"general"`` (multi-kernel CUDA-core path), ``"prefill"`` (the
-    tensor-core path at any M) or ``"direct"`` (the direct-streaming decode
-    kernel wherever it applies, the staged one otherwise)."""
-    _check(load_library().w4a16_set_path({"auto": 0, "general": 1, "prefill": 2, "direct": 3}[path]),
-           "w4a16_set_path")
+    tensor-core path at any M), ``"direct"`` (the direct-streaming decode
+    kernel wherever it applies, the staged one otherwise), ``"sliced"`` (the
+    expert-sliced decode kernel, M <= 4) or ``"staged"`` (the staged decode
+    kernel even where the expert-sliced one applies)."""
+    codes = {"auto": 0, "general": 1, "prefill": 2, "direct": 3, "sliced": 4, "staged": 5}
+    _check(load_library().w4a16_set_path(codes[path]), "w4a16_set_path")
 
 
 def read_status(hidden_shape: tuple[int, int], topk: int, num_experts: int, intermediate: int,
