@@ -203,11 +203,56 @@ def routed_layer_to_cpu(layer: dict, ids):
     return sub, remap[ids.to(torch.int64)]
 
 
+def decode_workload(M: int) -> str:
+    cfg = 1 if M == 1 else (2 if M <= 256 else 3)
+    return f"decode M={M} (config {cfg}): E=256 top-10 H=3072 I=1024 int4 g32, one layer"
+
+
+EP_WORKLOAD = ("config 4: expert-parallel stack of 4 MoE layers (E=256 top-10 H=3072 I=1024 int4 g32), "
+               "8192 tokens per step, Zipf(1.1)-biased routing")
+
+
+def run_reference_ep(args, world: int) -> int:
+    """Reference arm of configuration 4: the numpy oracle port (the reference's
+    per-expert fp32 dequant-then-GEMM, bench/bench_moe.py:run_reference) on all
+    host cores, timed on a bounded sample of tokens of one layer and scaled to
+    the 4-layer stack; the reference has no multi-GPU path."""
+    import torch
+
+    from kernels.synthetic import make_hidden, make_layer, make_routing, zipf_bias
+
+    sub_tok = 8
+    lay = make_layer(E // world, H, I, seed=0, device="cpu")
+    bias = zipf_bias(E, 1.1, seed=0)
+    tw, ids = make_routing(EP_TOKENS // world, E, TOPK, seed=0, device="cpu", bias=bias)
+    tw, ids = tw[:sub_tok], ids[:sub_tok] % (E // world)  # route into the generated experts
+    x = make_hidden(EP_TOKENS // world, H, seed=0, device="cpu")[:sub_tok]
+    sub, local_ids = routed_layer_to_cpu(lay, ids)
+    cores = os.cpu_count() or 1
+    cpu_port_time(sub_tok, sub, x, tw, local_ids, cores, 0.0, 1)
+    per, n = cpu_port_time(sub_tok, sub, x, tw, local_ids, cores, 20.0, max(args.steps, 3))
+    tps = sub_tok / per / EP_LAYERS
+    line = {
+        "impl": "reference", "metric": "ep_tokens_per_s", "value": tps, "unit": "tokens/s", "n_gpus": world,
+        "steps": n, "warmup": args.warmup, "ms_per_step": EP_TOKENS / tps * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": EP_WORKLOAD, "tokens_per_step": EP_TOKENS, "layers": EP_LAYERS},
+        "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{n} numpy-oracle forwards of one layer for {sub_tok} tokens (per-call "
+                                   f"dequant of their routed experts), scaled to the 4-layer stack"},
+        "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_reference_arm(args) -> int:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    if args.workload == "ep":
+        return run_reference_ep(args, world)
     import torch
 
     from kernels.synthetic import make_hidden, make_layer, make_routing
@@ -230,8 +275,8 @@ def run_reference_arm(args) -> int:
         "impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": world,
         "steps": n, "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"decode M={M} (config 1): E=256 top-10 H=3072 I=1024 int4 g32",
-                   "M": M, "unique_experts": n_act, "weight_bytes_per_step": wbytes},
+        "config": {"workload": decode_workload(M), "M": M, "unique_experts": n_act,
+                   "weight_bytes_per_step": wbytes},
         "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port",
                          "sample": f"{n} full forwards of the numpy oracle (restating bench/bench_moe.py:"
                                    f"run_reference, per-call dequant) at M={M} on the routed experts"},
@@ -379,7 +424,7 @@ def run_ours(args) -> int:
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"decode M={M} (config 1): E=256 top-10 H=3072 I=1024 int4 g32, one layer",
+            "config": {"workload": decode_workload(M),
                        "M": M, "unique_experts": n_act, "weight_bytes_per_step": wbytes,
                        "us_per_layer": 1e3 * total_ms / args.steps,
                        "stage_us": {"align": 1e3 * sum(align_ms) / len(align_ms), "w13": 1e3 * w13_mean,
@@ -482,6 +527,64 @@ def run_ep(args) -> int:
     e2e_ms = _max_over_ranks(t0.elapsed_time(t1), world)
     assert torch.isfinite(out.float()).all()
 
+    # ---- per-stage breakdown (separate, untimed pass with stage events) ----
+    nst = len(ep.EP_STAGES)
+    stage_ms = [0.0] * nst
+    reps = min(args.steps, 5)
+    for _ in range(reps):
+        x = x0
+        for l in range(EP_LAYERS):
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(nst + 1)]
+            x = ep.moe_layer(x, routing[l][0], routing[l][1], layers[l], E, emap, stage_events=evs)
+            evs[-1].synchronize()
+            for i in range(nst):
+                stage_ms[i] += evs[i].elapsed_time(evs[i + 1]) / (reps * EP_LAYERS)
+    stage_us = {name: 1e3 * _max_over_ranks(v, world) for name, v in zip(ep.EP_STAGES, stage_ms)}
+    # expert load: rows and routed slots this rank's experts receive per layer
+    recv_rows = sum(sum(ep.plan(routing[l][1], E).recv_counts) for l in range(EP_LAYERS)) / EP_LAYERS
+    max_recv_rows = _max_over_ranks(float(recv_rows), world)
+    mean_recv_rows = _sum_over_ranks(float(recv_rows), world) / world
+    # communicator check: every rank sees the same world through NCCL
+    comm_ok = True
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.ones(1, device=dev)
+        dist.all_reduce(t)
+        comm_ok = int(t.item()) == world == dist.get_world_size()
+
+    # ---- parity spot check (rank 0, untimed): layer 0 on 4 of its tokens vs the oracle ----
+    parity = None
+    if rank == 0 and not args.no_parity:
+        import numpy as np
+
+        from oracle import moe_oracle as O
+
+        x1 = ep.moe_layer(x0, routing[0][0], routing[0][1], layers[0], E, emap)
+        sub_tok = 4
+        ids_s = routing[0][1][:sub_tok].to(torch.int64).cpu()
+        tw_s = routing[0][0][:sub_tok].float().cpu().numpy()
+        per = E // world
+        used = torch.unique(ids_s)
+        ws = {k: [] for k in ("w1_q", "w1_s", "w2_q", "w2_s")}
+        owners = sorted({int(e) // per for e in used})
+        cpu_layers = {r: make_layer(per, H, I, seed=1000 * 0 + r, device="cpu") for r in owners}
+        for e in used.tolist():
+            lay = cpu_layers[e // per]
+            for k in ws:
+                ws[k].append(lay[k][e % per])
+        bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+        w1 = torch.stack(ws["w1_q"]).numpy()
+        s1 = bits(torch.stack(ws["w1_s"]))
+        w2 = torch.stack(ws["w2_q"]).numpy()
+        s2 = bits(torch.stack(ws["w2_s"]))
+        local = np.searchsorted(used.numpy(), ids_s.numpy())
+        ref = O.moe_reference(x0[:sub_tok].float().cpu().numpy(), w1, s1, w2, s2, tw_s, local, GROUP)
+        got = x1[:sub_tok].float().cpu().numpy()
+        parity = {"tokens": sub_tok, "layer": 0, "rel_frobenius": float(O.rel_frobenius(got, ref)),
+                  "max_abs": float(O.max_abs_err(got, ref)), "tol_rel_frobenius": 1e-2}
+        assert parity["rel_frobenius"] <= 1e-2, parity
+
     peaks = _peaks()
     flops = EP_LAYERS * EP_TOKENS * TOPK * FLOP_PER_SLOT  # whole job per step
     per_gpu_tflops = flops / world / (total_ms / args.steps * 1e-3) / 1e12
@@ -503,13 +606,15 @@ def run_ep(args) -> int:
             "metric": "ep_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "config 4: expert-parallel stack of 4 MoE layers (E=256 top-10 H=3072 I=1024 "
-                                   "int4 g32), 8192 tokens per step, Zipf(1.1)-biased routing",
+            "config": {"workload": EP_WORKLOAD,
                        "tokens_per_step": EP_TOKENS, "layers": EP_LAYERS, "experts_per_rank": len(own),
                        "parallelism": f"ep{world}",
                        "l2": "inputs larger than L2 (each layer's expert weights stream from HBM)",
                        "timing": "CUDA events around all steps on each rank, max over ranks",
-                       "nvlink_bytes_per_step_max_rank": max_sent},
+                       "nvlink_bytes_per_step_max_rank": max_sent,
+                       "stage_us_per_layer_max_rank": stage_us,
+                       "recv_rows_per_layer": {"max_rank": max_recv_rows, "mean": mean_recv_rows},
+                       "comm_nranks_ok": comm_ok, "parity_spot_check": parity},
             "e2e": {"value": EP_TOKENS * args.steps / (e2e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": m_src * H * 2, "d2h_bytes_per_step": m_src * H * 2,
                     "ms_per_step": e2e_ms / args.steps},
@@ -538,11 +643,16 @@ def main(argv=None) -> int:
     ap.add_argument("--M", type=int, default=1, help="tokens per step (config 1: 1)")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline sampling")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["decode", "ep"], default="decode",
-                    help="decode: configs 1-3 (--M); ep: config 4, expert-parallel over the ranks")
+    ap.add_argument("--workload", choices=["decode", "ep"], default=None,
+                    help="decode: configs 1-3 (--M); ep: config 4, expert-parallel over the ranks "
+                         "(default: ep when launched by torchrun, decode otherwise)")
+    ap.add_argument("--no-parity", action="store_true", help="skip the untimed parity spot check")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3
+    if args.workload is None:
+        # launched by torchrun (WORLD_SIZE set): the multi-GPU configuration 4
+        args.workload = "ep" if "WORLD_SIZE" in os.environ else "decode"
     if args.impl == "reference":
         return run_reference_arm(args)
     if args.workload == "ep":

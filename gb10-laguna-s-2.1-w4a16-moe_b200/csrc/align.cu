@@ -195,7 +195,6 @@ __global__ void __launch_bounds__(kAlignThreads, 1) moe_align_kernel(AlignParams
 //      grid-strided.
 // Slot order inside an expert is the flat slot order, as in the single-CTA
 // kernel: chunks, then warps, then lanes are all in ascending slot order.
-constexpr long long kAlignBarrierBudget = 2000000000LL;  // SM clocks
 
 __global__ void __launch_bounds__(kAlignThreads, 1) moe_align_grid_kernel(AlignParams p) {
   extern __shared__ int smem[];
@@ -206,7 +205,7 @@ __global__ void __launch_bounds__(kAlignThreads, 1) moe_align_grid_kernel(AlignP
   int* s_base = s_cnt + E;                // [E] this chunk's first rank per expert
   int* tot = s_base + E;                  // [C][E] chunk totals (copied from scratch)
   __shared__ int warp_tot[33];
-  __shared__ int s_gen;
+  __shared__ int s_gen, s_timeout;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int chunk = (p.n_tok + C - 1) / C;
@@ -216,7 +215,10 @@ __global__ void __launch_bounds__(kAlignThreads, 1) moe_align_grid_kernel(AlignP
 
   // 1. histograms
   for (int i = tid; i < kAlignWarps * E; i += kAlignThreads) hist[i] = 0;
-  if (tid == 0) s_gen = ld_acquire_gpu(p.grid_bar + 1);
+  if (tid == 0) {
+    s_gen = ld_acquire_gpu(p.grid_bar + 1);
+    s_timeout = 0;
+  }
   __syncthreads();
   for (int i = beg + lane; i < end; i += 32) {
     const int e = load_expert(p, i);
@@ -244,6 +246,7 @@ __global__ void __launch_bounds__(kAlignThreads, 1) moe_align_grid_kernel(AlignP
   // 2. grid barrier (arrival counter reset by the last arriver; generation word
   //    only increases, so the barrier needs no cleaning between launches)
   __syncthreads();
+  if (p.withhold && c == 0) return;  // test hook: this CTA never arrives
   if (tid == 0) {
     __threadfence();
     const int arrived = atomicAdd(p.grid_bar, 1) + 1;
@@ -254,8 +257,11 @@ __global__ void __launch_bounds__(kAlignThreads, 1) moe_align_grid_kernel(AlignP
     } else {
       const long long t0 = clock64();
       while (ld_acquire_gpu(p.grid_bar + 1) == s_gen) {
-        if (clock64() - t0 > kAlignBarrierBudget) {
-          atomicOr(p.grid_bar + 2, 1);  // error word: barrier timed out
+        if (clock64() - t0 > p.budget) {
+          // the totals are incomplete: report and write no outputs
+          atomicOr(p.grid_bar + 2, kAlignErrBarrier);
+          if (p.status != nullptr) atomicOr(p.status, kAlignErrBarrier);
+          s_timeout = 1;
           break;
         }
         __nanosleep(64);
@@ -264,6 +270,7 @@ __global__ void __launch_bounds__(kAlignThreads, 1) moe_align_grid_kernel(AlignP
     __threadfence();
   }
   __syncthreads();
+  if (s_timeout) return;
 
   // 3. chunk totals -> per-expert counts, this chunk's bases, padded offsets
   for (int i = tid; i < C * E; i += kAlignThreads) tot[i] = __ldcg(p.scratch + i);
@@ -388,7 +395,9 @@ int align_grid_ctas(int n_tok, int E, int sms) {
 // Scratch the multi-CTA variant needs: chunk totals + the 3-word barrier.
 size_t align_grid_scratch_ints(int E, int sms) { return (size_t)align_grid_max_ctas(E, sms) * E; }
 
-cudaError_t launch_align_grid(const AlignParams& p, int ctas, cudaStream_t stream) {
+cudaError_t launch_align_grid(const AlignParams& p_in, int ctas, cudaStream_t stream) {
+  AlignParams p = p_in;
+  if (p.budget <= 0) p.budget = kAlignBarrierBudget;
   const size_t smem = (size_t)(kAlignWarps * p.E + 3 * p.E + 1 + ctas * p.E) * sizeof(int);
   static thread_local size_t configured[64] = {0};
   int dev = 0;

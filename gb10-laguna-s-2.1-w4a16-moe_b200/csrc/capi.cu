@@ -65,6 +65,9 @@ thread_local cudaEvent_t g_stage_events[8];
 // Testing hook: route every forward through the general (multi-kernel) path.
 thread_local int g_force_general = 0;
 thread_local int g_n_stage_events = 0;
+// Test hook: 1 = multi-CTA align launches withhold CTA 0's barrier arrival and
+// wait ~10 us (the timeout path runs without any fault).
+thread_local int g_wait_test = 0;
 
 void mark_stage(int i, cudaStream_t st) {
   if (i >= g_n_stage_events || g_stage_events[i] == nullptr) return;
@@ -170,6 +173,29 @@ int w4a16_moe_read_status(const void* workspace, int64_t M, int64_t topk, int64_
   return kOk;
 }
 
+int w4a16_set_wait_test(int mode) {
+  g_last_error.clear();
+  if (mode < 0 || mode > 1) return fail(kInvalidArgument, "w4a16_set_wait_test: mode 0 or 1");
+  g_wait_test = mode;
+  return kOk;
+}
+
+int w4a16_moe_align_read_status(void* scratch, int32_t* status_out, void* stream) {
+  g_last_error.clear();
+  if (!scratch || !status_out) return fail(kInvalidArgument, "w4a16_moe_align_read_status: null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  int32_t* bar = (int32_t*)scratch;
+  cudaError_t err = cudaMemcpyAsync(status_out, bar + 2, sizeof(int32_t), cudaMemcpyDeviceToHost, st);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(st);
+  // arrivals of a barrier that timed out never reached the CTA count: clear
+  // the arrival counter and the error word (the generation word only grows)
+  if (err == cudaSuccess && *status_out != 0) err = cudaMemsetAsync(bar, 0, sizeof(int32_t), st);
+  if (err == cudaSuccess) err = cudaMemsetAsync(bar + 2, 0, sizeof(int32_t), st);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(st);
+  if (err != cudaSuccess) return cuda_fail(err, "w4a16_moe_align_read_status");
+  return kOk;
+}
+
 int w4a16_set_stage_events(void* const* events, int n_events) {
   g_last_error.clear();
   if (n_events < 0 || n_events > 8 || (n_events > 0 && events == nullptr))
@@ -225,6 +251,10 @@ int w4a16_moe_align_ex(const void* topk_ids, int ids_is_int64, int64_t M, int64_
   const int ctas = scratch != nullptr ? align_grid_ctas(p.n_tok, p.E, sm_count()) : 0;
   if (ctas > 0 && scratch_bytes >= w4a16_moe_align_scratch_bytes(p.n_tok, p.E)) {
     p.grid_bar = (int32_t*)scratch;
+    if (g_wait_test == 1) {
+      p.withhold = 1;
+      p.budget = 20000;
+    }
     p.scratch = (int32_t*)((char*)scratch + 256);
     err = launch_align_grid(p, ctas, (cudaStream_t)stream);
   } else {
@@ -326,8 +356,6 @@ int w4a16_moe_forward(const void* hidden, int64_t M, int64_t H, int64_t hidden_l
 #ifdef W4A16_DIAGNOSTICS
     if (const char* tr = getenv("W4A16_SLICED_TRACE")) sp.trace = (long long*)strtoull(tr, nullptr, 0);
     if (const char* tc = getenv("W4A16_SLICED_TRACE_CTA")) sp.trace_cta = atoi(tc);
-    if (const char* dg = getenv("W4A16_SLICED_DIAG")) sp.diag = atoi(dg);
-    if (const char* wn = getenv("W4A16_SLICED_WAIT_NS")) sp.wait_ns = atoi(wn);
 #endif
     if (sliced_plan(sp, sm_count(), max_smem_optin() - 1024)) {
       mark_stage(0, st);
@@ -420,6 +448,7 @@ int w4a16_moe_forward(const void* hidden, int64_t M, int64_t H, int64_t hidden_l
   if (align_ctas > 0 && (int64_t)align_grid_scratch_ints((int)E, sm_count()) * 4 <= 4 * n_tok * H) {
     ap.scratch = (int32_t*)ws.partial;
     ap.grid_bar = ws.align_bar;
+    ap.status = ws.sched + 2;
     err = launch_align_grid(ap, align_ctas, st);
   } else {
     err = launch_align(ap, st);

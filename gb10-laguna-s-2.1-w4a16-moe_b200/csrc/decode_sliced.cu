@@ -25,16 +25,20 @@
 //     (fp32 in shared memory, experts in ascending order); a row tile split
 //     between CTAs is finished by the CTA holding its last expert, which adds
 //     the other CTAs' fp32 pieces in CTA order (deterministic).
-//   * one producer warp streams every stage (w13 pair parts, w2 tile groups)
-//     with cp.async.bulk into a byte-granular shared-memory ring, in schedule
-//     order; w2 weights therefore stream while w13 is still computing.
-//   * 16 consumer warps decode int4 from the ring straight into m16n8k16 A
-//     fragments (code - 8 exact in bf16; the bf16 group scale is applied to the
-//     fp32 partial of each 32-wide group); token rows (hidden, intermediate)
-//     live in shared memory in a lane-permuted layout (two 16-byte loads give a
-//     lane its B fragments for a 64-wide chunk).
-//   * one epilogue warp reduces the 16 consumer warps' partials in fixed warp
-//     order, applies SiLU*up (w13) or the router weight (w2), publishes.
+//   * the CTA's schedule is a table of items (a w13 pair, or up to four w2 row
+//     tiles of one expert), built once in the prologue.  Each of the 16
+//     consumer warps walks every item, taking the 64-wide k-chunks warp,
+//     warp + 16, ...: it streams its own weight and scale blocks with cp.async
+//     into a private shared-memory ring kSlDepth groups ahead (so at any moment
+//     the CTA reads a contiguous stretch of each tile), decodes int4 straight
+//     into m16n8k16 A fragments (code - 8 exact in bf16; the bf16 group scale
+//     is applied to the fp32 partial of each 32-wide group), and meets the
+//     other warps only at the end of an item, in a double-buffered reduction
+//     buffer.  Token rows (hidden, intermediate) live in shared memory in a
+//     lane-permuted layout (two 16-byte loads give a lane its B fragments for
+//     a 64-wide chunk).
+//   * one epilogue warp reduces the 16 warps' partials of an item in fixed
+//     warp order, applies SiLU*up (w13) or the router weight (w2), publishes.
 //   * one loader warp waits (bounded) for each expert's readiness and copies
 //     its intermediate rows into shared memory.
 //
@@ -55,57 +59,44 @@ namespace w4moe {
 namespace {
 
 constexpr int kSlConsumers = 16;
-constexpr int kSlProducer = 16;  // warp index
-constexpr int kSlEpilogue = 17;
-constexpr int kSlLoader = 18;
-constexpr int kSlThreads = 19 * 32;
-constexpr int kSlNSB = 32;              // stage barrier slots (== warp width: lane k tracks slot k)
-constexpr int kSlMaxTiles = 4;          // row tiles per stage
-constexpr int kSlChunks = 16;           // k-chunks per w13 stage
+constexpr int kSlEpilogue = 16;  // warp index
+constexpr int kSlLoader = 17;
+constexpr int kSlThreads = 18 * 32;
+constexpr int kSlDepth = 4;             // cp.async groups in flight per consumer warp
+constexpr int kSlMaxTiles = 4;          // row tiles per w2 item
 constexpr long long kSlBudget = 4000000000LL;  // ~2 s of SM clocks
 constexpr int kSlMaxA = kSlicedMaxSlots;        // active experts <= slots
 
 // error bits in the workspace status word (sched[2])
-constexpr int kSlErrFull = 1 << 8, kSlErrEmpty = 1 << 9, kSlErrRed = 1 << 10, kSlErrReady = 1 << 11,
-              kSlErrInter = 1 << 12, kSlErrPiece = 1 << 13;
+constexpr int kSlErrRed = 1 << 10, kSlErrReady = 1 << 11, kSlErrInter = 1 << 12, kSlErrPiece = 1 << 13;
 
 struct SlCtx {
-  int A, P, G, c, chA, chB, nparts, NR, T2, lag, nrt2;
+  int A, P, G, c, chA, chB, NR, T2, lag, nrt2;
   int S0, S1;
 };
 
-// One pipeline stage of the CTA's schedule: its descriptor (consumers read it
-// from s_desc) and up to four global source ranges (producer only).
+// One item of the CTA's schedule.
 struct SlEntry {
-  int4 meta;              // x: type | ntile << 4 | gend << 8 | ae << 16; y: tile0 | c0 << 16; z: nch; w: bytes
-  const uint8_t* src[4];  // w13: gate w, up w, gate s, up s; w2: weights, scales
+  int4 meta;  // y: type (0 = w13 pair, 1 = w2 tiles) | ntile << 4 | ae << 16; z: tile0; w: nch
 };
 
 // Round in which the last pair of active expert e is computed.
 __host__ __device__ __forceinline__ int sl_ready_round(int e, int P, int G) { return ((e + 1) * P - 1) / G; }
 
 // w2 row tiles [ra, rb] of active expert ae inside the CTA's unit range [S0, S1)
-__host__ __device__ __forceinline__ void sl_w2_tiles(int ae, int A, long long S0, long long S1, int& ra, int& rb) {
-  ra = S0 <= ae ? 0 : (int)((S0 - ae + A - 1) / A);
-  rb = S1 - 1 < ae ? -1 : (int)((S1 - 1 - ae) / A);
+__host__ __device__ __forceinline__ void sl_w2_tiles(int ae, int A, int S0, int S1, int& ra, int& rb) {
+  ra = S0 <= ae ? 0 : (S0 - ae + A - 1) / A;
+  rb = S1 - 1 < ae ? -1 : (S1 - 1 - ae) / A;
 }
 
 __device__ __forceinline__ void sl_record(int32_t* sched, int code) { atomicOr(sched + 2, code); }
 
-// Bounded mbarrier wait that also gives up once the CTA is aborting.  Between
-// checks the warp is parked by try_wait's suspend hint (or by nanosleep when
-// sleep_ns > 0).
-__device__ __forceinline__ bool sl_wait(uint64_t* bar, uint32_t parity, const volatile int* abort_flag,
-                                        int sleep_ns = 0) {
+// Bounded mbarrier wait that also gives up once the CTA is aborting.
+__device__ __forceinline__ bool sl_wait(uint64_t* bar, uint32_t parity, const volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   for (;;) {
-    if (sleep_ns > 0) {
-      __nanosleep(sleep_ns);
-      if (mbar_try_wait(bar, parity)) return true;
-    } else if (mbar_try_wait_sleep(bar, parity, 2000u)) {
-      return true;
-    }
+    if (mbar_try_wait_sleep(bar, parity, 2000u)) return true;
     if (*abort_flag) return false;
     if (clock64() - t0 > kSlBudget) return false;
   }
@@ -116,6 +107,13 @@ __device__ __forceinline__ void red_release_add(int32_t* p, int v) {
 }
 __device__ __forceinline__ void st_release(int32_t* p, int v) {
   asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 
 // Lane-permuted position of element i of a token row: inside each 64-wide
@@ -160,20 +158,19 @@ __device__ __forceinline__ void sl_trace(long long* tr, int kind, int k) {
 
 // First w2 unit (row-tile-major numbering r * A + e) of CTA c: contiguous
 // ranges sized so that every CTA streams the same weight bytes, counting a
-// w13 pair as 2*chA chunk blocks and a w2 tile as chB.
-__host__ __device__ long long sliced_w2_start(int c, int A, int P, int G, int chA, int chB, int nrt2) {
-  const long long T2 = (long long)A * nrt2;
-  const long long pairs = (long long)A * P;
-  const long long rem = pairs % G;
+// w13 pair as 2*chA chunk blocks and a w2 tile as chB.  All intermediate
+// values stay below 2^31 for the shapes sliced_plan accepts.
+__host__ __device__ int sliced_w2_start(int c, int A, int P, int G, int chA, int chB, int nrt2) {
+  const int T2 = A * nrt2;
+  const int rem = (A * P) % G;
   if (rem == 0) return T2 * c / G;
-  const long long W2 = T2 * chB, X = 2LL * chA * (G - rem);
+  const int W2 = T2 * chB, X = 2 * chA * (G - rem);
   if (W2 <= X) return c <= rem ? 0 : T2 * (c - rem) / (G - rem);  // CTAs with the extra pair take no w2
-  const long long lo = c < rem ? c : rem, hi = c > rem ? c - rem : 0;
-  return (lo * (W2 - X) + hi * (W2 - X + 2LL * chA * G)) / ((long long)G * chB);
+  const int lo = c < rem ? c : rem, hi = c > rem ? c - rem : 0;
+  return (lo * (W2 - X) + hi * (W2 - X + 2 * chA * G)) / (G * chB);
 }
 
 __global__ void __launch_bounds__(kSlThreads, 1) moe_decode_sliced_kernel(SlicedParams p) {
-  __shared__ uint64_t full_bar[kSlNSB], empty_bar[kSlNSB];
   __shared__ uint64_t red_full[2], red_empty[2], inter_bar[kSlMaxA], pc_bar;
   __shared__ int s_tok[kSlicedMaxSlots], s_eid[kSlicedMaxSlots], s_first[kSlicedMaxSlots];
   __shared__ float s_wt[kSlicedMaxSlots], s_wt_in[kSlicedMaxSlots];
@@ -183,7 +180,6 @@ __global__ void __launch_bounds__(kSlThreads, 1) moe_decode_sliced_kernel(Sliced
   __shared__ int s_pc[kSlicedMaxPieces];
   __shared__ int s_npc;
   __shared__ volatile int s_abort;
-  __shared__ int4 s_desc[kSlNSB], s_gdesc[2];
   extern __shared__ __align__(128) unsigned char dsm[];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -196,13 +192,13 @@ __global__ void __launch_bounds__(kSlThreads, 1) moe_decode_sliced_kernel(Sliced
   float* const red = reinterpret_cast<float*>(dsm + p.off_red);    // [2][16 warps][maxT][16][Mp]
   float* const oacc = reinterpret_cast<float*>(dsm + p.off_oacc);  // [nr_cap][M][16]
   float* const pcs = reinterpret_cast<float*>(dsm + p.off_pc);     // [pc_cap][M][16]
-  SlEntry* const table = reinterpret_cast<SlEntry*>(dsm + p.off_table);  // [max_stages + 1]
+  SlEntry* const table = reinterpret_cast<SlEntry*>(dsm + p.off_table);  // [max_stages]
   int* const rscratch = reinterpret_cast<int*>(dsm + p.off_rounds);      // [3][max_rounds + 1]
-  unsigned char* const ring = dsm + p.off_ring;                          // [n_slots][slot_bytes]
+  unsigned char* const ring = dsm + p.off_ring;                          // [16 warps][kSlDepth][slot_bytes]
   const int xstride = H * 2 + 16, istride = I * 2 + 16;
   const int Mp = p.Mp, maxT = p.maxT;
   const int red_warp = maxT * 16 * Mp;  // floats per warp in one buffer
-  const int nslots = p.n_slots, slot_bytes = p.slot_bytes;
+  const int slot_bytes = p.slot_bytes;
 
   // ---------------- prologue ----------------
   if (tid == 0) sl_trace(tr, 4, 0);
@@ -212,15 +208,17 @@ __global__ void __launch_bounds__(kSlThreads, 1) moe_decode_sliced_kernel(Sliced
     // router weight is their sum (in slot order), so an expert has at most M
     // columns.  Columns are ordered by expert, then token; active experts
     // ascending.
+    // Each slot gets the key e * 64 + token (or -1): keys order columns,
+    // equal keys share a column, key >> 6 is the expert.
     const int n = p.n_tok;
-    int e_l[2], m_l[2];
+    int k_l[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int i = lane + 32 * h;
-      e_l[h] = i < n ? p.map(i) : -1;
-      m_l[h] = i / p.topk;
+      const int e = i < n ? p.map(i) : -1;
+      k_l[h] = e >= 0 ? (e << 6) | (i / p.topk) : -1;
       if (i < n) {
-        s_eid[i] = e_l[h];
+        s_eid[i] = k_l[h];
         s_wt_in[i] = p.topk_w[i];
       }
     }
@@ -229,15 +227,16 @@ __global__ void __launch_bounds__(kSlThreads, 1) moe_decode_sliced_kernel(Sliced
     for (int h = 0; h < 2; ++h) {
       const int i = lane + 32 * h;
       if (i < n) {
-        // bit 0: first slot of its (expert, token) column; bit 1: of its expert
+        // bit 0: first slot of its column; bit 1: first slot of its expert
+        const int k = k_l[h];
         int same_e = 0, same_col = 0;
 #pragma unroll 8
         for (int jj = 0; jj < i; ++jj) {
-          const int ej = s_eid[jj];
-          same_e |= ej == e_l[h];
-          same_col |= (ej == e_l[h]) & (jj / p.topk == m_l[h]);
+          const int kj = s_eid[jj];
+          same_col |= kj == k;
+          same_e |= (kj >> 6) == (k >> 6);
         }
-        s_first[i] = e_l[h] >= 0 ? ((same_col ? 0 : 1) | (same_e ? 0 : 2)) : 0;
+        s_first[i] = k >= 0 ? ((same_col ? 0 : 1) | (same_e ? 0 : 2)) : 0;
       }
     }
     __syncwarp();
@@ -245,25 +244,25 @@ __global__ void __launch_bounds__(kSlThreads, 1) moe_decode_sliced_kernel(Sliced
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int i = lane + 32 * h;
-      const int e = e_l[h];
-      const bool mine = i < n && e >= 0 && (s_first[i] & 1);
-      int below = 0, same_before = 0, same = 0, act_below = 0;
+      const int k = k_l[h], e = k >> 6;
+      const bool mine = i < n && k >= 0 && (s_first[i] & 1);
+      int col = 0, below = 0, same = 0, act_below = 0;
       float wsum = 0.f;
 #pragma unroll 8
       for (int jj = 0; jj < n; ++jj) {
-        const int ej = s_eid[jj];
+        const int kj = s_eid[jj];
         const int fj = s_first[jj];
-        const bool valid = ej >= 0;
-        const bool col1 = valid && (fj & 1);
-        below += col1 && ej < e;
-        same += col1 && ej == e;
-        same_before += col1 && ej == e && jj < i;
-        act_below += valid && ej < e && (fj & 2);
-        if (valid && ej == e && jj / p.topk == m_l[h]) wsum += s_wt_in[jj];
+        const int ej = kj >> 6;
+        if (fj & 1) {
+          col += kj < k;
+          below += ej < e;
+          same += ej == e;
+        }
+        act_below += (fj & 2) && ej < e;
+        if (kj == k) wsum += s_wt_in[jj];
       }
       if (mine) {
-        const int col = below + same_before;
-        s_tok[col] = m_l[h];
+        s_tok[col] = k & 63;
         s_wt[col] = wsum;
         if (s_first[i] & 2) {
           s_act[act_below] = e;
@@ -279,10 +278,6 @@ __global__ void __launch_bounds__(kSlThreads, 1) moe_decode_sliced_kernel(Sliced
     }
   } else if (warp == kSlLoader) {
     // barriers, initialised lane-parallel
-    for (int s = lane; s < kSlNSB; s += 32) {
-      mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], kSlConsumers);
-    }
     for (int a = lane; a < kSlMaxA; a += 32) mbar_init(&inter_bar[a], 1);
     if (lane < 2) {
       mbar_init(&red_full[lane], kSlConsumers);
@@ -294,7 +289,7 @@ __global__ void __launch_bounds__(kSlThreads, 1) moe_decode_sliced_kernel(Sliced
     }
     fence_barrier_init();
   } else {
-    // hidden rows -> shared memory, lane-permuted (warps 1..17)
+    // hidden rows -> shared memory, lane-permuted (warps 1..16)
     const int h8 = H / 8, nthr = (kSlLoader - 1) * 32, me = tid - 32;
     for (int idx = me; idx < M * h8; idx += nthr) {
       const int m = idx / h8, k8 = idx - m * h8;
@@ -324,138 +319,23 @@ __global__ void __launch_bounds__(kSlThreads, 1) moe_decode_sliced_kernel(Sliced
   x.c = c;
   x.chA = H / 64;
   x.chB = I / 64;
-  x.nparts = (x.chA + kSlChunks - 1) / kSlChunks;
   x.NR = (A * x.P + G - 1) / G;
   x.T2 = p.T2;
   x.lag = p.lag;
   x.nrt2 = H / 16;
-  x.S0 = (int)sliced_w2_start(c, A, x.P, G, x.chA, x.chB, x.nrt2);
-  x.S1 = (int)sliced_w2_start(c + 1, A, x.P, G, x.chA, x.chB, x.nrt2);
+  x.S0 = sliced_w2_start(c, A, x.P, G, x.chA, x.chB, x.nrt2);
+  x.S1 = sliced_w2_start(c + 1, A, x.P, G, x.chA, x.chB, x.nrt2);
   const int r_lo = x.S1 > x.S0 ? x.S0 / A : 0;
   const int r_hi = x.S1 > x.S0 ? (x.S1 - 1) / A : -1;
 
-  if (warp < kSlConsumers) {
-    // ======================= consumer warps =======================
-    float acc[kSlMaxTiles][4];
-#pragma unroll
-    for (int tt = 0; tt < kSlMaxTiles; ++tt) acc[tt][0] = acc[tt][1] = acc[tt][2] = acc[tt][3] = 0.f;
-    int si = 0, gi = 0;
-    for (;;) {
-      const int slot = si % nslots;
-      if (!sl_wait(&full_bar[slot], (si / nslots) & 1, &s_abort, p.wait_ns)) {
-        if (lane == 0 && !s_abort) sl_record(p.sched, kSlErrFull);
-        s_abort = 1;
-        break;
-      }
-      if (warp == 0 && lane == 0) sl_trace(tr, 5, si);
-      const int4 d = s_desc[slot];
-      const int type = d.y & 15;
-      const int ntile = (d.y >> 4) & 15, gend = (d.y >> 8) & 1, ae = d.y >> 16;
-      const int tile0 = d.z & 0xFFFF, c0 = d.z >> 16, nch = d.w;
-      if (type != 2) {
-        const int cnt = s_cnt[ae], base = s_base[ae];
-        const unsigned char* brow = nullptr;
-        if (type == 0) {
-          if (g < cnt) brow = xs + (size_t)s_tok[base + g] * xstride;
-        } else {
-          if (!(p.diag & 4) && !sl_wait(&inter_bar[ae], 0, &s_abort)) {
-            if (lane == 0 && !s_abort) sl_record(p.sched, kSlErrInter);
-            s_abort = 1;
-            break;
-          }
-          if (g < cnt) brow = inter_s + (size_t)(base + g) * istride;
-        }
-        const unsigned char* wb = ring + (size_t)slot * slot_bytes;
-        const int nblk = ntile * nch;
-        const unsigned char* sb = wb + (size_t)nblk * 512;
-        uint4 q0 = make_uint4(0, 0, 0, 0), q1 = q0;
-        if (p.diag & 1) {
-          // diagnostics: pipeline only, no math
-        } else if ((nch & 15) == 0) {
-          for (int ch = warp; ch < nch; ch += kSlConsumers) {
-            if (brow != nullptr) {
-              q0 = lds128(brow + (size_t)(c0 + ch) * 128 + t * 32);
-              q1 = lds128(brow + (size_t)(c0 + ch) * 128 + t * 32 + 16);
-            }
-#pragma unroll
-            for (int tt = 0; tt < kSlMaxTiles; ++tt) {
-              if (tt < ntile) {
-                const int i = tt * nch + ch;
-                const uint4 wv = lds128(wb + (size_t)i * 512 + lane * 16);
-                const uint2 sv = lds64(sb + (size_t)i * 64 + g * 8);
-                sl_block(acc[tt], wv, sv, q0, q1);
-              }
-            }
-          }
-        } else {
-          int bch = -1;
-          for (int i = warp; i < nblk; i += kSlConsumers) {
-            const int tile = i / nch, ch = i - tile * nch;
-            if (ch != bch) {
-              if (brow != nullptr) {
-                q0 = lds128(brow + (size_t)(c0 + ch) * 128 + t * 32);
-                q1 = lds128(brow + (size_t)(c0 + ch) * 128 + t * 32 + 16);
-              }
-              bch = ch;
-            }
-            const uint4 wv = lds128(wb + (size_t)i * 512 + lane * 16);
-            const uint2 sv = lds64(sb + (size_t)i * 64 + g * 8);
-            float pd[4] = {0.f, 0.f, 0.f, 0.f};
-            sl_block(pd, wv, sv, q0, q1);
-#pragma unroll
-            for (int tt = 0; tt < kSlMaxTiles; ++tt)
-              if (tt == tile) {
-                acc[tt][0] += pd[0];
-                acc[tt][1] += pd[1];
-                acc[tt][2] += pd[2];
-                acc[tt][3] += pd[3];
-              }
-          }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty_bar[slot]);
-        if (warp == 0 && lane == 0) sl_trace(tr, 1, si);
-        (void)tile0;
-      }
-      if (type == 2 || gend) {
-        const int b = gi & 1;
-        if (gi >= 2 && !sl_wait(&red_empty[b], ((gi >> 1) - 1) & 1, &s_abort)) {
-          if (lane == 0 && !s_abort) sl_record(p.sched, kSlErrRed);
-          s_abort = 1;
-          break;
-        }
-        if (type != 2) {
-          float* rw = red + (size_t)b * kSlConsumers * red_warp + (size_t)warp * red_warp;
-          if (2 * t < Mp) {
-#pragma unroll
-            for (int tt = 0; tt < kSlMaxTiles; ++tt)
-              if (tt < ntile) {
-                *reinterpret_cast<float2*>(rw + (tt * 16 + g) * Mp + 2 * t) = make_float2(acc[tt][0], acc[tt][1]);
-                *reinterpret_cast<float2*>(rw + (tt * 16 + g + 8) * Mp + 2 * t) =
-                    make_float2(acc[tt][2], acc[tt][3]);
-              }
-          }
-#pragma unroll
-          for (int tt = 0; tt < kSlMaxTiles; ++tt) acc[tt][0] = acc[tt][1] = acc[tt][2] = acc[tt][3] = 0.f;
-        }
-        if (warp == 0 && lane == 0) s_gdesc[b] = d;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&red_full[b]);
-        ++gi;
-        if (type == 2) break;
-      }
-      ++si;
-    }
-  } else if (warp == kSlProducer) {
-    // ======================= producer warp =======================
-    // Builds the CTA's stage table once (lane-parallel), then streams it:
-    // stage s uses ring slot and barrier s % n_slots.  Order: round j's w13
-    // pair stages, then the w2 stages of the experts inserted after round j
-    // (ascending expert), and after the last round the remaining experts.
-    int* const rcnt = rscratch;                    // [NR + 1] stages per round
-    int* const r13 = rscratch + p.max_rounds + 1;  // [NR + 1] w13 stages per round
-    int* const rstart = r13 + p.max_rounds + 1;    // [NR + 1] first stage of each round
-    const int nrt13 = 2 * x.P, NR = x.NR;
+  if (warp == kSlEpilogue) {
+    // The CTA's item table, built lane-parallel: round j's w13 pair, then the
+    // w2 items of the experts inserted after round j (ascending expert), and
+    // after the last round the remaining experts.
+    int* const rcnt = rscratch;                    // [NR + 1] items per round
+    int* const r13 = rscratch + p.max_rounds + 1;  // [NR + 1] w13 items per round
+    int* const rstart = r13 + p.max_rounds + 1;    // [NR + 1] first item of each round
+    const int NR = x.NR;
     for (int ae = lane; ae < A; ae += 32) {
       int ra, rb;
       sl_w2_tiles(ae, A, x.S0, x.S1, ra, rb);
@@ -465,7 +345,7 @@ __global__ void __launch_bounds__(kSlThreads, 1) moe_decode_sliced_kernel(Sliced
     }
     __syncwarp();
     for (int j = lane; j <= NR; j += 32) {
-      const int c13 = (j < NR && x.c + j * G < A * x.P) ? x.nparts : 0;
+      const int c13 = (j < NR && x.c + j * G < A * x.P) ? 1 : 0;
       int c2 = 0;
       for (int ae = 0; ae < A; ++ae) c2 += s_w2ins[ae] == j ? s_w2n[ae] : 0;
       rcnt[j] = c13 + c2;
@@ -481,22 +361,10 @@ __global__ void __launch_bounds__(kSlThreads, 1) moe_decode_sliced_kernel(Sliced
       s_nst = run;
     }
     __syncwarp();
-    const int nst = s_nst;
     for (int j = lane; j < NR; j += 32) {
       if (r13[j] == 0) continue;
-      const int q = x.c + j * G, ae = q / x.P, pr = q - ae * x.P, e = s_act[ae];
-      for (int k = 0; k < x.nparts; ++k) {
-        const int c0 = k * kSlChunks, nch = min(kSlChunks, x.chA - c0);
-        const size_t bg = ((size_t)e * nrt13 + pr) * x.chA + c0;
-        const size_t bu = ((size_t)e * nrt13 + x.P + pr) * x.chA + c0;
-        SlEntry en;
-        en.meta = make_int4(2 * nch * 576, 0 | (2 << 4) | ((k == x.nparts - 1) << 8) | (ae << 16), pr | (c0 << 16), nch);
-        en.src[0] = p.w13 + bg * 512;
-        en.src[1] = p.w13 + bu * 512;
-        en.src[2] = p.s13 + bg * 64;
-        en.src[3] = p.s13 + bu * 64;
-        table[rstart[j] + k] = en;
-      }
+      const int q = x.c + j * G, ae = q / x.P, pr = q - ae * x.P;
+      table[rstart[j]].meta = make_int4(0, 0 | (2 << 4) | (ae << 16), pr, x.chA);
     }
     for (int ae = lane; ae < A; ae += 32) {
       const int j = s_w2ins[ae];
@@ -504,67 +372,127 @@ __global__ void __launch_bounds__(kSlThreads, 1) moe_decode_sliced_kernel(Sliced
       for (int a2 = 0; a2 < ae; ++a2) pos += s_w2ins[a2] == j ? s_w2n[a2] : 0;
       int ra, rb;
       sl_w2_tiles(ae, A, x.S0, x.S1, ra, rb);
-      const int e = s_act[ae];
       for (int r = ra; r <= rb; r += x.T2) {
         const int nt = min(x.T2, rb - r + 1);
-        const size_t b0 = ((size_t)e * x.nrt2 + r) * x.chB;
-        SlEntry en;
-        en.meta = make_int4(nt * x.chB * 576, 1 | (nt << 4) | (1 << 8) | (ae << 16), r, x.chB);
-        en.src[0] = p.w2 + b0 * 512;
-        en.src[1] = p.s2 + b0 * 64;
-        en.src[2] = nullptr;
-        en.src[3] = nullptr;
-        table[pos++] = en;
+        table[pos++].meta = make_int4(0, 1 | (nt << 4) | (ae << 16), r, x.chB);
       }
     }
-    __syncwarp();
-    if (lane == 0) sl_trace(tr, 4, 6);
-    const uint64_t pol = l2_evict_first_policy();
+  }
+  __syncthreads();
+  if (tid == 0) sl_trace(tr, 4, 6);
+  const int nitems = s_nst;
+
+  if (warp < kSlConsumers) {
+    // ======================= consumer warps =======================
+    // Group = one k-chunk of one item (all of its row tiles); this warp's
+    // groups are the chunks warp, warp + 16, ... of every item, streamed with
+    // cp.async kSlDepth groups ahead into the warp's private ring.
+    unsigned char* const wring = ring + (size_t)warp * kSlDepth * slot_bytes;
+    const int nrt13 = 2 * x.P;
+    int iss_it = 0, iss_ch = warp, iss_n = 0;  // issue cursor; groups issued
+    auto issue_next = [&]() {
+      while (iss_it < nitems) {
+        const int4 m = table[iss_it].meta;
+        if (iss_ch < m.w) break;
+        ++iss_it;
+        iss_ch = warp;
+      }
+      if (iss_it < nitems) {
+        const int4 m = table[iss_it].meta;
+        const int type = m.y & 15, nt = (m.y >> 4) & 15, e = s_act[m.y >> 16], ch = iss_ch;
+        unsigned char* const dst = wring + (size_t)(iss_n % kSlDepth) * slot_bytes;
+#pragma unroll
+        for (int tt = 0; tt < kSlMaxTiles; ++tt) {
+          if (tt < nt) {
+            size_t blk;
+            const uint8_t *wsrc, *ssrc;
+            if (type == 0) {
+              blk = ((size_t)e * nrt13 + (tt == 0 ? 0 : x.P) + m.z) * x.chA + ch;
+              wsrc = p.w13;
+              ssrc = p.s13;
+            } else {
+              blk = ((size_t)e * x.nrt2 + m.z + tt) * x.chB + ch;
+              wsrc = p.w2;
+              ssrc = p.s2;
+            }
+            cp_async16(dst + tt * 512 + lane * 16, wsrc + blk * 512 + lane * 16);
+            if (lane < 8) cp_async8(dst + nt * 512 + tt * 64 + lane * 8, ssrc + blk * 64 + lane * 8);
+          }
+        }
+        ++iss_n;
+        iss_ch += kSlConsumers;
+      }
+      cp_async_commit();
+    };
+#pragma unroll 1
+    for (int k = 0; k < kSlDepth; ++k) issue_next();
+
+    float acc[kSlMaxTiles][4];
+#pragma unroll
+    for (int tt = 0; tt < kSlMaxTiles; ++tt) acc[tt][0] = acc[tt][1] = acc[tt][2] = acc[tt][3] = 0.f;
+    int cons_n = 0;
     bool ok = true;
-    int s = 0;
-    for (; s <= nst; ++s) {
-      const int slot = s % nslots;
-      if (s >= nslots && !sl_wait(&empty_bar[slot], ((s / nslots) - 1) & 1, &s_abort)) {
-        if (lane == 0 && !s_abort) sl_record(p.sched, kSlErrEmpty);
+    for (int it = 0; it < nitems && ok; ++it) {
+      const int4 m = table[it].meta;
+      const int type = m.y & 15, nt = (m.y >> 4) & 15, ae = m.y >> 16, nch = m.w;
+      const int cnt = s_cnt[ae], base = s_base[ae];
+      const unsigned char* brow = nullptr;
+      if (type == 0) {
+        if (g < cnt) brow = xs + (size_t)s_tok[base + g] * xstride;
+      } else if (warp < nch) {
+        if (!sl_wait(&inter_bar[ae], 0, &s_abort)) {
+          if (lane == 0 && !s_abort) sl_record(p.sched, kSlErrInter);
+          s_abort = 1;
+          ok = false;
+          break;
+        }
+        if (g < cnt) brow = inter_s + (size_t)(base + g) * istride;
+      }
+      for (int ch = warp; ch < nch; ch += kSlConsumers) {
+        cp_async_wait_group<kSlDepth - 1>();
+        __syncwarp();
+        const unsigned char* const sl = wring + (size_t)(cons_n % kSlDepth) * slot_bytes;
+        uint4 q0 = make_uint4(0, 0, 0, 0), q1 = q0;
+        if (brow != nullptr) {
+          q0 = lds128(brow + (size_t)ch * 128 + t * 32);
+          q1 = lds128(brow + (size_t)ch * 128 + t * 32 + 16);
+        }
+#pragma unroll
+        for (int tt = 0; tt < kSlMaxTiles; ++tt) {
+          if (tt < nt) {
+            const uint4 wv = lds128(sl + tt * 512 + lane * 16);
+            const uint2 sv = lds64(sl + nt * 512 + tt * 64 + g * 8);
+            sl_block(acc[tt], wv, sv, q0, q1);
+          }
+        }
+        __syncwarp();  // every lane is done with the slot before it is refilled
+        ++cons_n;
+        issue_next();
+      }
+      // end of item: partials to the epilogue
+      const int b = it & 1;
+      if (it >= 2 && !sl_wait(&red_empty[b], ((it >> 1) - 1) & 1, &s_abort)) {
+        if (lane == 0 && !s_abort) sl_record(p.sched, kSlErrRed);
         s_abort = 1;
         ok = false;
         break;
       }
-      if (s == nst) {  // end mark
-        if (lane == 0) {
-          s_desc[slot] = make_int4(0, 2, 0, 0);
-          mbar_arrive(&full_bar[slot]);
-        }
-        break;
+      float* rw = red + (size_t)b * kSlConsumers * red_warp + (size_t)warp * red_warp;
+      if (2 * t < Mp) {
+#pragma unroll
+        for (int tt = 0; tt < kSlMaxTiles; ++tt)
+          if (tt < nt) {
+            *reinterpret_cast<float2*>(rw + (tt * 16 + g) * Mp + 2 * t) = make_float2(acc[tt][0], acc[tt][1]);
+            *reinterpret_cast<float2*>(rw + (tt * 16 + g + 8) * Mp + 2 * t) = make_float2(acc[tt][2], acc[tt][3]);
+          }
       }
-      const int4 meta = table[s].meta;
-      if (lane == 0) {
-        s_desc[slot] = meta;
-        mbar_arrive_expect_tx(&full_bar[slot], (uint32_t)meta.x);
-      }
+#pragma unroll
+      for (int tt = 0; tt < kSlMaxTiles; ++tt) acc[tt][0] = acc[tt][1] = acc[tt][2] = acc[tt][3] = 0.f;
       __syncwarp();
-      const int type = meta.y & 15, nt = (meta.y >> 4) & 15, nch = meta.w;
-      unsigned char* const dst = ring + (size_t)slot * slot_bytes;
-      if (lane < (type == 0 ? 4 : 2)) {
-        uint32_t off, sz;
-        if (type == 0) {
-          const uint32_t wb = (uint32_t)nch * 512, sb = (uint32_t)nch * 64;
-          off = lane < 2 ? lane * wb : 2 * wb + (lane - 2) * sb;
-          sz = lane < 2 ? wb : sb;
-        } else {
-          const uint32_t wb = (uint32_t)(nt * nch) * 512;
-          off = lane == 0 ? 0u : wb;
-          sz = lane == 0 ? wb : (uint32_t)(nt * nch) * 64;
-        }
-        bulk_g2s_hint(dst + off, table[s].src[lane], sz, &full_bar[slot], pol);
-      }
-      if (lane == 0) sl_trace(tr, 0, s);
+      if (lane == 0) mbar_arrive(&red_full[b]);
+      if (warp == 0 && lane == 0) sl_trace(tr, 1, it);
     }
-    // copies still in flight must land before the CTA may exit (the slot
-    // that took the end mark held a stage that was already consumed)
-    const int issued = s < nst ? s : nst;
-    const int first = ok ? max(0, issued - nslots + 1) : max(0, issued - nslots);
-    for (int k = first; k < issued; ++k) mbar_wait(&full_bar[k % nslots], (k / nslots) & 1, kSlBudget);
+    cp_async_wait_group<0>();  // nothing in flight into the ring when the warp exits
   } else if (warp == kSlEpilogue) {
     // ======================= epilogue warp =======================
     const int nloc = r_hi >= r_lo ? r_hi - r_lo + 1 : 0;
@@ -574,9 +502,9 @@ __global__ void __launch_bounds__(kSlThreads, 1) moe_decode_sliced_kernel(Sliced
     // that tile's last expert
     const bool has_np = x.S1 > x.S0 && ((x.S1 - 1) % A) != A - 1;
     const int np_e = has_np ? (x.S1 - 1) % A : -1;
-    int gi = 0;
+    const int nitems = s_nst;
     bool ok = true;
-    for (;;) {
+    for (int gi = 0; gi < nitems; ++gi) {
       const int b = gi & 1;
       if (!sl_wait(&red_full[b], (gi >> 1) & 1, &s_abort)) {
         if (lane == 0 && !s_abort) sl_record(p.sched, kSlErrRed);
@@ -584,9 +512,8 @@ __global__ void __launch_bounds__(kSlThreads, 1) moe_decode_sliced_kernel(Sliced
         ok = false;
         break;
       }
-      const int4 d = s_gdesc[b];
+      const int4 d = table[gi].meta;
       const int type = d.y & 15;
-      if (type == 2) break;
       const int ntile = (d.y >> 4) & 15, ae = d.y >> 16, tile0 = d.z & 0xFFFF;
       const float* rb = red + (size_t)b * kSlConsumers * red_warp;
       const int cnt = s_cnt[ae], base = s_base[ae];
@@ -629,7 +556,6 @@ __global__ void __launch_bounds__(kSlThreads, 1) moe_decode_sliced_kernel(Sliced
         }
       }
       if (lane == 0) sl_trace(tr, 2, gi);
-      ++gi;
     }
     // own row tiles and the combined first row tile -> bf16 output
     if (ok) {
@@ -654,6 +580,7 @@ __global__ void __launch_bounds__(kSlThreads, 1) moe_decode_sliced_kernel(Sliced
       }
     }
     if (lane == 0) sl_trace(tr, 4, 2);
+    if (lane == 0) sl_trace(tr, 4, 2);
   } else if (warp == kSlLoader) {
     // ======================= loader warp =======================
     const bool has_comb = x.S1 > x.S0 && x.S0 % A != 0 && x.S1 - 1 >= r_lo * A + A - 1 &&
@@ -667,10 +594,10 @@ __global__ void __launch_bounds__(kSlThreads, 1) moe_decode_sliced_kernel(Sliced
         if (lane == 0) {
           int n = 0;
           int lst[kSlicedMaxPieces];
-          const long long tile_start = (long long)r_lo * A;
+          const int tile_start = r_lo * A;
           for (int cc = c - 1; cc >= 0 && n < kSlicedMaxPieces; --cc) {
-            const long long a0 = sliced_w2_start(cc, A, x.P, G, x.chA, x.chB, x.nrt2);
-            const long long a1 = sliced_w2_start(cc + 1, A, x.P, G, x.chA, x.chB, x.nrt2);
+            const int a0 = sliced_w2_start(cc, A, x.P, G, x.chA, x.chB, x.nrt2);
+            const int a1 = sliced_w2_start(cc + 1, A, x.P, G, x.chA, x.chB, x.nrt2);
             if (a1 <= tile_start) break;
             if (a1 > a0) lst[n++] = cc;
           }
@@ -770,16 +697,16 @@ struct SlPlanKeyHash {
   }
 };
 struct SlBounds {
-  int nr, pc, stages, rounds;
+  int nr, pc, items, rounds;
 };
 
 // Largest number of w2 row tiles any CTA touches, of pieces any combiner
-// adds, of stages in any CTA's schedule and of w13 rounds, over every
+// adds, of items in any CTA's schedule and of w13 rounds, over every
 // possible active-expert count.
 SlBounds sliced_bounds(int n_tok, int E, int H, int I, int G, int T2) {
   static std::mutex mu;
   static std::unordered_map<SlPlanKey, SlBounds, SlPlanKeyHash> cache;
-  const SlPlanKey key{n_tok, E, H, I, G};
+  const SlPlanKey key{n_tok, E, H, I, G * 8 + T2};
   {
     std::lock_guard<std::mutex> lk(mu);
     auto it = cache.find(key);
@@ -787,28 +714,27 @@ SlBounds sliced_bounds(int n_tok, int E, int H, int I, int G, int T2) {
   }
   SlBounds b{1, 0, 0, 0};
   const int P = I / 16, chA = H / 64, chB = I / 64, nrt2 = H / 16;
-  const int nparts = (chA + kSlChunks - 1) / kSlChunks;
   const int amax = n_tok < E ? n_tok : E;
-  std::vector<long long> S(G + 1);
+  std::vector<int> S(G + 1);
   for (int A = 1; A <= amax; ++A) {
     for (int cc = 0; cc <= G; ++cc) S[cc] = sliced_w2_start(cc, A, P, G, chA, chB, nrt2);
     b.rounds = std::max(b.rounds, (A * P + G - 1) / G);
     for (int cc = 0; cc < G; ++cc) {
-      int nst = nparts * ((A * P - cc + G - 1) / G);
+      int n = (A * P - cc + G - 1) / G;
       for (int ae = 0; ae < A; ++ae) {
         int ra, rb;
         sl_w2_tiles(ae, A, S[cc], S[cc + 1], ra, rb);
-        if (rb >= ra) nst += (rb - ra + 1 + T2 - 1) / T2;
+        if (rb >= ra) n += (rb - ra + 1 + T2 - 1) / T2;
       }
-      b.stages = std::max(b.stages, nst);
+      b.items = std::max(b.items, n);
       if (S[cc + 1] <= S[cc]) continue;
-      const long long rl = S[cc] / A, rh = (S[cc + 1] - 1) / A;
-      b.nr = std::max<int>(b.nr, (int)(rh - rl + 1));
+      const int rl = S[cc] / A, rh = (S[cc + 1] - 1) / A;
+      b.nr = std::max(b.nr, rh - rl + 1);
       // pieces preceding this CTA's first row tile
-      int n = 0;
+      int np = 0;
       for (int c2 = cc - 1; c2 >= 0 && S[c2 + 1] > rl * A; --c2)
-        if (S[c2 + 1] > S[c2]) ++n;
-      b.pc = std::max(b.pc, n);
+        if (S[c2 + 1] > S[c2]) ++np;
+      b.pc = std::max(b.pc, np);
     }
   }
   std::lock_guard<std::mutex> lk(mu);
@@ -822,47 +748,58 @@ int sliced_plan(SlicedParams& p, int sms, int max_smem) {
   if (p.M < 1 || p.M > kSlicedMaxM || p.n_tok > kSlicedMaxSlots || p.n_tok < 1) return 0;
   if (p.H % 64 || p.I % 64) return 0;
   const int chA = p.H / 64, chB = p.I / 64;
-  if (chB > 64 || p.H / 16 > 65535) return 0;
   if (sms > kSlicedMaxGrid) sms = kSlicedMaxGrid;
+  // the w2 range arithmetic runs in 32-bit integers
+  const long long amax = std::min<long long>(p.n_tok, p.E);
+  if (amax * (p.H / 16) * chB * (long long)sms * 2 + 2LL * chA * sms * sms >= (1LL << 31)) return 0;
+  if (amax * (p.I / 16) >= (1LL << 15)) return 0;
   p.grid = sms;
   p.Mp = p.M <= 2 ? 2 : 4;
-  // ring slots fit one w13 stage (gate + up, <= 16 chunks) or T2 w2 row tiles
-  const int w13_stage = 2 * std::min(kSlChunks, chA) * 576;
-  p.T2 = std::max(1, std::min(kSlMaxTiles, w13_stage / (chB * 576)));
   p.lag = 1;
+  auto up = [](int v) { return (v + 127) / 128 * 128; };
+  const int static_smem = 6144;  // barriers + routing tables (static shared memory of the kernel)
+  // the largest w2 item (row tiles per item) whose consumer rings still fit
+  bool fits = false;
+  for (p.T2 = kSlMaxTiles; p.T2 >= 1 && !fits; p.T2 >>= 1) {
+#ifdef W4A16_DIAGNOSTICS
+    if (const char* e = getenv("W4A16_SLICED_T2"))
+      if (p.T2 > atoi(e)) continue;
+#endif
+    p.maxT = std::max(2, p.T2);
+    p.slot_bytes = up(p.maxT * 576);
+    const SlBounds b = sliced_bounds(p.n_tok, p.E, p.H, p.I, p.grid, p.T2);
+    if (b.pc > kSlicedMaxPieces) return 0;
+    p.nr_cap = b.nr;
+    p.max_stages = b.items;
+    p.max_rounds = b.rounds;
+    int off = 0;
+    p.off_x = off;
+    off += up(p.M * (p.H * 2 + 16));
+    p.off_inter = off;
+    off += up(p.n_tok * (p.I * 2 + 16));
+    p.off_red = off;
+    off += up(2 * kSlConsumers * p.maxT * 16 * p.Mp * 4);
+    p.off_oacc = off;
+    off += up(p.nr_cap * p.M * 16 * 4);
+    p.off_pc = off;
+    off += up(std::max(1, b.pc) * p.M * 16 * 4);
+    p.off_table = off;
+    off += up(std::max(1, p.max_stages) * (int)sizeof(SlEntry));
+    p.off_rounds = off;
+    off += up(3 * (p.max_rounds + 1) * 4);
+    p.off_ring = off;
+    p.n_slots = kSlDepth;
+    p.ring_bytes = kSlConsumers * kSlDepth * p.slot_bytes;
+    p.smem_bytes = off + p.ring_bytes;
+    if (p.smem_bytes + static_smem <= max_smem) {
+      fits = true;
+      break;
+    }
+  }
+  if (!fits) return 0;
 #ifdef W4A16_DIAGNOSTICS
   if (const char* e = getenv("W4A16_SLICED_LAG")) p.lag = atoi(e);
-  if (const char* e = getenv("W4A16_SLICED_T2")) p.T2 = std::max(1, std::min(p.T2, atoi(e)));
 #endif
-  p.maxT = std::max(2, p.T2);
-  p.slot_bytes = (std::max(w13_stage, p.T2 * chB * 576) + 127) / 128 * 128;
-  const SlBounds b = sliced_bounds(p.n_tok, p.E, p.H, p.I, p.grid, p.T2);
-  if (b.pc > kSlicedMaxPieces) return 0;
-  p.nr_cap = b.nr;
-  p.max_stages = b.stages;
-  p.max_rounds = b.rounds;
-  auto up = [](int v) { return (v + 127) / 128 * 128; };
-  int off = 0;
-  p.off_x = off;
-  off += up(p.M * (p.H * 2 + 16));
-  p.off_inter = off;
-  off += up(p.n_tok * (p.I * 2 + 16));
-  p.off_red = off;
-  off += up(2 * kSlConsumers * p.maxT * 16 * p.Mp * 4);
-  p.off_oacc = off;
-  off += up(p.nr_cap * p.M * 16 * 4);
-  p.off_pc = off;
-  off += up(std::max(1, b.pc) * p.M * 16 * 4);
-  p.off_table = off;
-  off += up((p.max_stages + 1) * (int)sizeof(SlEntry));
-  p.off_rounds = off;
-  off += up(3 * (p.max_rounds + 1) * 4);
-  p.off_ring = off;
-  const int static_smem = 6144;  // barriers + routing tables (static shared memory of the kernel)
-  p.n_slots = std::min(kSlNSB, (max_smem - off - static_smem) / p.slot_bytes);
-  if (p.n_slots < 3) return 0;
-  p.ring_bytes = p.n_slots * p.slot_bytes;
-  p.smem_bytes = off + p.ring_bytes;
   return 1;
 }
 

@@ -27,7 +27,12 @@ struct AlignParams {
   // multi-CTA variant only
   int32_t* scratch;         // [C * E] chunk totals
   int32_t* grid_bar;        // [3] zero-initialised: arrivals, generation, error word
+  int32_t* status;          // nullable: a barrier timeout is also OR-ed in here
+  long long budget;         // grid-barrier wait limit in SM clocks
+  int withhold;             // test hook: CTA 0 does not arrive at the barrier
 };
+constexpr long long kAlignBarrierBudget = 2000000000LL;  // SM clocks (~1 s)
+constexpr int kAlignErrBarrier = 1 << 16;  // status bit: align grid barrier timed out
 cudaError_t launch_align(const AlignParams& p, cudaStream_t stream);
 int align_grid_ctas(int n_tok, int E, int sms);
 size_t align_grid_scratch_ints(int E, int sms);
@@ -125,8 +130,6 @@ struct SlicedParams {
   int32_t* sched;            // status word at [2]
   long long* trace;          // optional pipeline timestamps of CTA trace_cta (diagnostics)
   int trace_cta;
-  int diag;                  // diagnostics: bit 0 = skip the math (pipeline only)
-  int wait_ns;               // > 0: consumers back off with nanosleep between barrier checks
   // plan (sliced_plan)
   int grid, smem_bytes, Mp, T2, maxT, lag, nr_cap;
   int off_x, off_inter, off_red, off_oacc, off_pc, off_table, off_rounds, off_ring, ring_bytes;
@@ -134,7 +137,7 @@ struct SlicedParams {
 };
 int sliced_plan(SlicedParams& p, int sms, int max_smem);
 cudaError_t launch_sliced(const SlicedParams& p, cudaStream_t stream);
-__host__ __device__ long long sliced_w2_start(int c, int A, int P, int G, int chA, int chB, int nrt2);
+__host__ __device__ int sliced_w2_start(int c, int A, int P, int G, int chA, int chB, int nrt2);
 
 // ---- prefill.cu (tcgen05 grouped GEMMs for large M) ----
 struct PrefillParams {

@@ -171,19 +171,36 @@ class LocalExperts:
     s2: torch.Tensor
 
 
+EP_STAGES = ("plan+counts", "pack", "dispatch", "experts", "return", "combine")
+
+
 def moe_layer(hidden: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor, experts: LocalExperts,
-              num_experts: int, expert_map: torch.Tensor, group=None) -> torch.Tensor:
+              num_experts: int, expert_map: torch.Tensor, group=None, stage_events=None) -> torch.Tensor:
     """One expert-parallel MoE layer for this rank's source tokens.
 
     ``topk_ids`` hold global expert ids.  Returns ``[M, H]`` bf16: the same
     result as a single-GPU :func:`fused_experts_w4a16` over all experts, up to
-    the bf16 rounding of each owner rank's partial sum.
+    the bf16 rounding of each owner rank's partial sum.  ``stage_events``
+    (optional, profiling): a list of ``len(EP_STAGES) + 1`` CUDA events recorded
+    on the current stream at the stage boundaries (plan and count exchange
+    with its host read, pack, row dispatch, local experts, row return,
+    combine).
     """
+    ev = stage_events
+
+    def mark(i):
+        if ev is not None:
+            ev[i].record()
+
     M, H = hidden.shape
+    mark(0)
     pl = plan(topk_ids, num_experts, group)
+    mark(1)
     x_send, meta_send = pack(hidden, topk_weights, topk_ids, pl)
+    mark(2)
     x_recv = exchange(x_send, pl.send_counts, pl.recv_counts, group)
     meta_recv = exchange(meta_send, pl.send_counts, pl.recv_counts, group)
+    mark(3)
     topk = topk_ids.shape[1]
     if x_recv.shape[0] > 0:
         ids_recv = meta_recv[:, :topk].contiguous()
@@ -192,5 +209,9 @@ def moe_layer(hidden: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.
                                    expert_map=expert_map, global_num_experts=num_experts)
     else:
         y = x_recv.new_empty((0, H))
+    mark(4)
     back = exchange(y, pl.recv_counts, pl.send_counts, group)
-    return combine(back, pl.tok_row, M, len(pl.send_counts), H)
+    mark(5)
+    out = combine(back, pl.tok_row, M, len(pl.send_counts), H)
+    mark(6)
+    return out

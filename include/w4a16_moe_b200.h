@@ -99,6 +99,23 @@ W4A16_API int w4a16_moe_align_ex(const void* topk_ids, int ids_is_int64, int64_t
                     int64_t scratch_bytes, void* stream);
 
 /*
+ * Status of the multi-CTA align kernels that used `scratch` (no reference
+ * counterpart).  *status_out receives the error bits of the calls since the
+ * last query (bit 16: the grid barrier timed out; that call wrote no
+ * outputs).  The query also resets the scratch's barrier words, so a scratch
+ * whose call timed out is usable again afterwards.  Synchronises `stream`.
+ */
+W4A16_API int w4a16_moe_align_read_status(void* scratch, int32_t* status_out, void* stream);
+
+/*
+ * Test hook for the bounded device waits (no reference counterpart): mode 1
+ * makes the calling thread's next multi-CTA align launches withhold one CTA's
+ * arrival at the grid barrier and wait only ~10 us, so the wait runs out and
+ * the timeout is reported as status; mode 0 restores normal operation.
+ */
+W4A16_API int w4a16_set_wait_test(int mode);
+
+/*
  * Load-time weight transform into this library's fragment-major layout.
  * Replaces repack_weights (kernels/w4a16_moe.py:63-116).
  *   w_q     (E, N_out, K/2) uint8        scales (E, N_out, K/group_size) bf16
