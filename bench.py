@@ -480,10 +480,12 @@ def run_ep(args) -> int:
         tw, ids = make_routing(m_src, E, TOPK, seed=7919 * l + 31 * rank, device=dev, bias=bias)
         routing.append((tw, ids))
     x0 = make_hidden(m_src, H, seed=rank, device=dev)
+    # fixed-capacity exchange (no host read of counts) unless asked otherwise
+    cap = m_src if args.ep_exchange == "fixed" else None
 
     def step(x):
         for l in range(EP_LAYERS):
-            x = ep.moe_layer(x, routing[l][0], routing[l][1], layers[l], E, emap)
+            x = ep.moe_layer(x, routing[l][0], routing[l][1], layers[l], E, emap, capacity=cap)
         return x
 
     for _ in range(max(args.warmup, 3)):
@@ -535,7 +537,7 @@ def run_ep(args) -> int:
         x = x0
         for l in range(EP_LAYERS):
             evs = [torch.cuda.Event(enable_timing=True) for _ in range(nst + 1)]
-            x = ep.moe_layer(x, routing[l][0], routing[l][1], layers[l], E, emap, stage_events=evs)
+            x = ep.moe_layer(x, routing[l][0], routing[l][1], layers[l], E, emap, stage_events=evs, capacity=cap)
             evs[-1].synchronize()
             for i in range(nst):
                 stage_ms[i] += evs[i].elapsed_time(evs[i + 1]) / (reps * EP_LAYERS)
@@ -560,7 +562,7 @@ def run_ep(args) -> int:
 
         from oracle import moe_oracle as O
 
-        x1 = ep.moe_layer(x0, routing[0][0], routing[0][1], layers[0], E, emap)
+        x1 = ep.moe_layer(x0, routing[0][0], routing[0][1], layers[0], E, emap, capacity=cap)
         sub_tok = 4
         ids_s = routing[0][1][:sub_tok].to(torch.int64).cpu()
         tw_s = routing[0][0][:sub_tok].float().cpu().numpy()
@@ -568,11 +570,15 @@ def run_ep(args) -> int:
         used = torch.unique(ids_s)
         ws = {k: [] for k in ("w1_q", "w1_s", "w2_q", "w2_s")}
         owners = sorted({int(e) // per for e in used})
-        cpu_layers = {r: make_layer(per, H, I, seed=1000 * 0 + r, device="cpu") for r in owners}
-        for e in used.tolist():
-            lay = cpu_layers[e // per]
-            for k in ws:
-                ws[k].append(lay[k][e % per])
+        for r in owners:  # the owner's layer-0 weights (same device generator), routed experts to host
+            lay = make_layer(per, H, I, seed=1000 * 0 + r, device=dev)
+            for e in used.tolist():
+                if e // per == r:
+                    for k in ws:
+                        ws[k].append((e, lay[k][e % per].cpu()))
+            del lay
+        for k in ws:  # ascending expert order, as `used`
+            ws[k] = [v for _, v in sorted(ws[k], key=lambda ev: ev[0])]
         bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
         w1 = torch.stack(ws["w1_q"]).numpy()
         s1 = bits(torch.stack(ws["w1_s"]))
@@ -608,7 +614,7 @@ def run_ep(args) -> int:
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": EP_WORKLOAD,
                        "tokens_per_step": EP_TOKENS, "layers": EP_LAYERS, "experts_per_rank": len(own),
-                       "parallelism": f"ep{world}",
+                       "parallelism": f"ep{world}", "exchange": args.ep_exchange,
                        "l2": "inputs larger than L2 (each layer's expert weights stream from HBM)",
                        "timing": "CUDA events around all steps on each rank, max over ranks",
                        "nvlink_bytes_per_step_max_rank": max_sent,
@@ -647,6 +653,8 @@ def main(argv=None) -> int:
                     help="decode: configs 1-3 (--M); ep: config 4, expert-parallel over the ranks "
                          "(default: ep when launched by torchrun, decode otherwise)")
     ap.add_argument("--no-parity", action="store_true", help="skip the untimed parity spot check")
+    ap.add_argument("--ep-exchange", choices=["fixed", "counts"], default="fixed",
+                    help="ep: fixed-capacity all-to-all (no host sync) or exact counts read back to the host")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3

@@ -489,8 +489,13 @@ int w4a16_moe_forward(const void* hidden, int64_t M, int64_t H, int64_t hidden_l
     if (const char* tr = getenv("W4A16_PREFILL_TRACE")) p13.trace = (long long*)strtoull(tr, nullptr, 0);
 #endif
     PrefillParams p2 = p13;
-    if (getenv("W4A16_PREFILL_TRACE_W2") == nullptr) p2.trace = nullptr;
-    else p13.trace = nullptr;
+    p2.trace = nullptr;
+#ifdef W4A16_DIAGNOSTICS
+    if (getenv("W4A16_PREFILL_TRACE_W2") != nullptr) {
+      p2.trace = p13.trace;
+      p13.trace = nullptr;
+    }
+#endif
     p2.w = (const uint8_t*)w2_rep;
     p2.s = (const uint8_t*)s2_rep;
     p2.n_rowtiles = (int)(H / 16);

@@ -671,10 +671,6 @@ int decode_plan(DecodeParams& p, int sms, int max_smem) {
   if (const char* e = getenv("W4A16_DECODE_RP")) RP = atoi(e);
   if (const char* e = getenv("W4A16_DECODE_R2")) R2 = atoi(e);
 #endif
-#ifdef W4A16_DIAGNOSTICS
-  if (const char* e = getenv("W4A16_DECODE_RP")) RP = atoi(e);
-  if (const char* e = getenv("W4A16_DECODE_R2")) R2 = atoi(e);
-#endif
   while (RP > 1 && (p.I / 16) % RP) RP >>= 1;
   while (R2 > 2 && (p.H / 16) % R2) R2 >>= 1;
   if ((p.H / 16) % R2 || (p.I / 16) % RP) return 0;

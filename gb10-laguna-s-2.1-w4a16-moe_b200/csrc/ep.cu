@@ -138,6 +138,96 @@ __global__ void ep_combine_kernel(const __nv_bfloat16* back, const int32_t* tok_
   }
 }
 
+
+// ---- fixed-capacity dispatch (no host read of the counts) ----
+// Every rank sends every rank a block of `cap` rows (cap >= the source batch,
+// a token goes to a rank at most once): block r holds, in ascending token
+// order, the tokens routed to rank r, then padding rows whose top-k ids are
+// -1 (they route nowhere).  A row is [hidden (H bf16) | top-k ids (int32) |
+// top-k weights (fp32 bits) | zero pad], row_stride bf16 elements, so one
+// all-to-all with equal splits moves rows and routing together.
+
+// One CTA per destination rank: ascending-token scan of "routed to rank r".
+__global__ void __launch_bounds__(kEpPlanThreads, 1)
+    ep_plan_fixed_kernel(const void* ids, int is64, int M, int topk, int E, int G, int cap, int32_t* counts,
+                         int32_t* send_tok, int32_t* tok_row) {
+  __shared__ int warp_tot[33];
+  __shared__ int s_base;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, r = blockIdx.x;
+  const int per = E / G;
+  if (tid == 0) s_base = 0;
+  __syncthreads();
+  for (int m0 = 0; m0 < M; m0 += kEpPlanThreads) {
+    const int m = m0 + tid;
+    int f = 0;
+    if (m < M) {
+      for (int t = 0; t < topk; ++t) {
+        const long long e = ep_id(ids, is64, (long long)m * topk + t);
+        if (e >= 0 && e < E && (int)(e / per) == r) f = 1;
+      }
+    }
+    int incl = f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += u;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      const int w = warp_tot[lane];
+      int wi = w;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, wi, o);
+        if (lane >= o) wi += u;
+      }
+      warp_tot[lane] = wi - w;
+      if (lane == 31) warp_tot[32] = wi;
+    }
+    __syncthreads();
+    const int pos = s_base + warp_tot[warp] + incl - f;
+    if (m < M) {
+      tok_row[(size_t)m * G + r] = f ? r * cap + pos : -1;
+      if (f) send_tok[(size_t)r * cap + pos] = m;
+    }
+    __syncthreads();
+    if (tid == 0) s_base += warp_tot[32];
+    __syncthreads();
+  }
+  if (tid == 0) counts[r] = s_base;
+}
+
+__global__ void ep_pack_fixed_kernel(const __nv_bfloat16* x, long long x_ld, const void* ids, int is64,
+                                     const float* w, int topk, int H, int G, int cap, int rs,
+                                     const int32_t* counts, const int32_t* send_tok, __nv_bfloat16* send) {
+  const int v_per_row = rs / 8, h8 = H / 8;
+  const long long total = (long long)G * cap * v_per_row;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int i = (int)(idx / v_per_row), v = (int)(idx - (long long)i * v_per_row);
+    const int r = i / cap, j = i - r * cap;
+    const bool valid = j < counts[r];
+    uint4* dst = reinterpret_cast<uint4*>(send + (size_t)i * rs) + v;
+    if (v < h8) {
+      if (valid) *dst = *reinterpret_cast<const uint4*>(x + (size_t)send_tok[i] * x_ld + v * 8);
+      continue;
+    }
+    // routing metadata: 4 int32 words per vector
+    const int m = valid ? send_tok[i] : 0;
+    uint32_t word[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int k = (v - h8) * 4 + q;
+      uint32_t val = 0;
+      if (k < topk) val = valid ? (uint32_t)(int32_t)ep_id(ids, is64, (long long)m * topk + k) : 0xFFFFFFFFu;
+      else if (k < 2 * topk) val = valid ? (uint32_t)__float_as_int(w[(size_t)m * topk + k - topk]) : 0u;
+      word[q] = val;
+    }
+    *dst = make_uint4(word[0], word[1], word[2], word[3]);
+  }
+}
+
 static int grid_for(long long work, int threads) {
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -178,6 +268,32 @@ W4A16_API int w4a16_ep_pack(const void* hidden, int64_t hidden_ld, const void* t
   ep_pack_kernel<<<grid_for(work, 256), 256, 0, (cudaStream_t)stream>>>(
       (const __nv_bfloat16*)hidden, hidden_ld, topk_ids, ids_is_int64, topk_weights, (int)topk, (int)H, send_offsets,
       (int)n_ranks, send_tok, (__nv_bfloat16*)x_send, meta_send);
+  const cudaError_t err = cudaGetLastError();
+  return err == cudaSuccess ? kOk : report_error(kCudaError, cudaGetErrorString(err));
+}
+
+
+W4A16_API int w4a16_ep_dispatch_fixed(const void* hidden, int64_t hidden_ld, const void* topk_ids, int ids_is_int64,
+                                      const float* topk_weights, int64_t M, int64_t topk, int64_t num_experts,
+                                      int64_t H, int64_t n_ranks, int64_t capacity, int64_t row_stride,
+                                      void* send_rows, int32_t* send_counts, int32_t* send_tok, int32_t* tok_row,
+                                      void* stream) {
+  if (M < 0 || topk <= 0 || H <= 0 || H % 8 != 0 || hidden_ld < H || n_ranks <= 0 || num_experts <= 0 ||
+      num_experts % n_ranks != 0 || capacity < M || capacity > (1 << 24) ||
+      row_stride < H + 4 * topk || row_stride % 8 != 0)
+    return report_error(kInvalidArgument,
+                        "w4a16_ep_dispatch_fixed: bad sizes (H % 8 == 0, capacity >= M, row_stride >= H + 4*topk "
+                        "and a multiple of 8, num_experts divisible by n_ranks)");
+  if ((M > 0 && (!hidden || !topk_ids || !topk_weights || !tok_row)) || !send_rows || !send_counts || !send_tok)
+    return report_error(kInvalidArgument, "w4a16_ep_dispatch_fixed: null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  ep_plan_fixed_kernel<<<(int)n_ranks, kEpPlanThreads, 0, st>>>(topk_ids, ids_is_int64, (int)M, (int)topk,
+                                                                 (int)num_experts, (int)n_ranks, (int)capacity,
+                                                                 send_counts, send_tok, tok_row);
+  const long long work = n_ranks * capacity * (row_stride / 8);
+  ep_pack_fixed_kernel<<<grid_for(work, 256), 256, 0, st>>>(
+      (const __nv_bfloat16*)hidden, hidden_ld, topk_ids, ids_is_int64, topk_weights, (int)topk, (int)H,
+      (int)n_ranks, (int)capacity, (int)row_stride, send_counts, send_tok, (__nv_bfloat16*)send_rows);
   const cudaError_t err = cudaGetLastError();
   return err == cudaSuccess ? kOk : report_error(kCudaError, cudaGetErrorString(err));
 }

@@ -94,4 +94,17 @@ int w4a16_moe_forward_noalloc(const void* hidden, int64_t M, int64_t H, int64_t 
                            global_num_experts, out, scratch, kNoAllocScratchBytes, stream);
 }
 
+// Error bits of the last w4a16_moe_forward_noalloc call of this shape on the
+// current device (bounded device waits that ran out), read from the static
+// scratch and then cleared.  Synchronises `stream`.
+int w4a16_moe_noalloc_read_status(int64_t M, int64_t topk, int64_t E, int64_t H, int64_t I, int32_t* status_out,
+                                  void* stream) {
+  if (w4a16_moe_workspace_size(M, topk, E, H, I) < 0)
+    return report_error(1, "w4a16_moe_noalloc_read_status: bad sizes (M, topk, E, H, I)");
+  void* scratch = nullptr;
+  if (noalloc_scratch(&scratch) != cudaSuccess)
+    return report_error(3, "w4a16_moe_noalloc_read_status: cudaGetSymbolAddress of the scratch array failed");
+  return w4a16_moe_read_status(scratch, M, topk, E, H, I, status_out, stream);
+}
+
 }  // extern "C"

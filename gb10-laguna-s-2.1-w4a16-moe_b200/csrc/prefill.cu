@@ -9,18 +9,21 @@
 //   A (M = 128) = 128 weight rows, dequantised in shared memory:
 //       w13 (MODE 0): 64 gate rows + the matching 64 up rows,
 //       w2  (MODE 1): 128 hidden rows;
-//   B (N <= 256) = the expert's routed token rows (hidden rows for w13,
-//       intermediate rows for w2), gathered with cp.async;
+//   B (N <= 256) = the expert's routed token rows, read with one 2-D tensor
+//       load (TMA) per 64-wide k-block from an expert-sorted copy of the
+//       rows (w13: a gather kernel writes the hidden rows in sorted order;
+//       w2: the w13 epilogue writes the intermediate in sorted order);
 //   D = A * B^T, 128 x N fp32 in tensor memory (two 256-column buffers, so
 //       the epilogue of one item overlaps the MMAs of the next).
 //
 // Work item = (active expert, 256-token chunk, weight row tile); items are
 // assigned round-robin (CTA b takes b, b+grid, ...).  Per 64-wide k-block:
-//   * 8 loader warps: cp.async the packed int4 block (8 row tiles x 512 B +
-//     scales) into a staging area and the token rows into the 128-byte-
-//     swizzled B tile (rows past the chunk are zero-filled), then decode the
-//     staged int4 into the swizzled bf16 A tile ((code - 8) * scale, rounded
-//     once to bf16 -- the reference's dequantised value).  Stages ahead: 3.
+//   * loader warps: 3-D tensor loads (TMA) of the packed int4 block (8 row
+//     tiles x 512 B + scales) into a staging area and 2-D tensor loads of the
+//     token rows into the 128-byte-swizzled B tile (rows past the chunk are
+//     zero-filled), then decode the staged int4 into the swizzled bf16 A tile
+//     ((code - 8) * scale, rounded once to bf16 -- the reference's
+//     dequantised value).
 //   * 1 MMA warp: one thread issues 4 tcgen05.mma (K = 16 each) per k-block
 //     and tcgen05.commit frees the stage when they complete.
 //   * 4 epilogue warps (one TMEM lane quarter each) read D with tcgen05.ld:

@@ -44,6 +44,9 @@ def _lib() -> ctypes.CDLL:
         lib.w4a16_ep_pack.restype = c_int
         lib.w4a16_ep_pack.argtypes = [c_vp, c_i64, c_vp, c_int, c_vp, c_i64, c_i64, c_i64, c_i64,
                                       c_vp, c_vp, c_vp, c_vp, c_vp]
+        lib.w4a16_ep_dispatch_fixed.restype = c_int
+        lib.w4a16_ep_dispatch_fixed.argtypes = [c_vp, c_i64, c_vp, c_int, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64,
+                                                c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp]
         lib.w4a16_ep_combine.restype = c_int
         lib.w4a16_ep_combine.argtypes = [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp]
         _BOUND = True
@@ -174,8 +177,70 @@ class LocalExperts:
 EP_STAGES = ("plan+counts", "pack", "dispatch", "experts", "return", "combine")
 
 
+def row_stride(H: int, topk: int) -> int:
+    """bf16 elements per fixed-capacity send row: hidden, then 2*topk int32 of routing."""
+    return H + (4 * topk + 7) // 8 * 8
+
+
+@dataclass
+class FixedDispatch:
+    """Send blocks of the fixed-capacity exchange (device tensors only)."""
+
+    send: torch.Tensor  # [G * capacity, row_stride] bf16
+    counts: torch.Tensor  # [G] int32 valid rows per block
+    send_tok: torch.Tensor  # [G * capacity] int32
+    tok_row: torch.Tensor  # [M * G] int32, returned row of (token, rank) or -1
+    capacity: int
+
+
+def dispatch_fixed(hidden: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor, num_experts: int,
+                   world: int, capacity: int) -> FixedDispatch:
+    """Plan + pack into ``world`` blocks of ``capacity`` rows (one GPU kernel
+    pair, no host synchronisation); routing metadata rides in each row."""
+    M, H = hidden.shape
+    topk = topk_ids.shape[1]
+    dev = hidden.device
+    rs = row_stride(H, topk)
+    ids = topk_ids if topk_ids.dtype in (torch.int32, torch.int64) else topk_ids.to(torch.int32)
+    ids = ids.contiguous()
+    tw = topk_weights.to(torch.float32).contiguous()
+    if hidden.stride(1) != 1:
+        hidden = hidden.contiguous()
+    send = torch.empty((world * capacity, rs), dtype=torch.bfloat16, device=dev)
+    counts = torch.empty(world, dtype=torch.int32, device=dev)
+    send_tok = torch.empty(max(world * capacity, 1), dtype=torch.int32, device=dev)
+    tok_row = torch.empty(max(M * world, 1), dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        _K._check(
+            _lib().w4a16_ep_dispatch_fixed(hidden.data_ptr(), hidden.stride(0), ids.data_ptr(),
+                                           1 if ids.dtype == torch.int64 else 0, tw.data_ptr(), M, topk,
+                                           num_experts, H, world, capacity, rs, send.data_ptr(), counts.data_ptr(),
+                                           send_tok.data_ptr(), tok_row.data_ptr(), _K._stream_ptr(dev)),
+            "w4a16_ep_dispatch_fixed",
+        )
+    return FixedDispatch(send, counts, send_tok, tok_row, capacity)
+
+
+def unpack_rows(rows: torch.Tensor, H: int, topk: int):
+    """(hidden view [N, H] with row stride, ids [N, topk] int32, weights [N, topk] fp32) of received rows."""
+    ids = rows[:, H:H + 2 * topk].contiguous().view(torch.int32)
+    w = rows[:, H + 2 * topk:H + 4 * topk].contiguous().view(torch.float32)
+    return rows[:, :H], ids, w
+
+
+def all_to_all_equal(x: torch.Tensor, group=None) -> torch.Tensor:
+    """All-to-all with equal splits (block r of x goes to rank r)."""
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    if world == 1:
+        return x
+    out = torch.empty_like(x)
+    dist.all_to_all_single(out, x, group=group)
+    return out
+
+
 def moe_layer(hidden: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor, experts: LocalExperts,
-              num_experts: int, expert_map: torch.Tensor, group=None, stage_events=None) -> torch.Tensor:
+              num_experts: int, expert_map: torch.Tensor, group=None, stage_events=None,
+              capacity: int | None = None) -> torch.Tensor:
     """One expert-parallel MoE layer for this rank's source tokens.
 
     ``topk_ids`` hold global expert ids.  Returns ``[M, H]`` bf16: the same
@@ -184,7 +249,9 @@ def moe_layer(hidden: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.
     (optional, profiling): a list of ``len(EP_STAGES) + 1`` CUDA events recorded
     on the current stream at the stage boundaries (plan and count exchange
     with its host read, pack, row dispatch, local experts, row return,
-    combine).
+    combine).  ``capacity`` (>= M, equal on every rank) selects the
+    fixed-capacity exchange: :func:`dispatch_fixed`, one all-to-all of rows
+    with their routing each way, no host synchronisation.
     """
     ev = stage_events
 
@@ -193,6 +260,9 @@ def moe_layer(hidden: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.
             ev[i].record()
 
     M, H = hidden.shape
+    if capacity is not None:
+        return _moe_layer_fixed(hidden, topk_weights, topk_ids, experts, num_experts, expert_map, group, mark,
+                                capacity)
     mark(0)
     pl = plan(topk_ids, num_experts, group)
     mark(1)
@@ -213,5 +283,26 @@ def moe_layer(hidden: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.
     back = exchange(y, pl.recv_counts, pl.send_counts, group)
     mark(5)
     out = combine(back, pl.tok_row, M, len(pl.send_counts), H)
+    mark(6)
+    return out
+
+
+def _moe_layer_fixed(hidden, topk_weights, topk_ids, experts, num_experts, expert_map, group, mark, capacity):
+    M, H = hidden.shape
+    topk = topk_ids.shape[1]
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    mark(0)
+    d = dispatch_fixed(hidden, topk_weights, topk_ids, num_experts, world, capacity)
+    mark(1)
+    mark(2)
+    recv = all_to_all_equal(d.send, group)
+    mark(3)
+    x_recv, ids_recv, w_recv = unpack_rows(recv, H, topk)
+    y = _K.fused_experts_w4a16(x_recv, experts.w13, experts.w2, experts.s13, experts.s2, w_recv, ids_recv,
+                               expert_map=expert_map, global_num_experts=num_experts)
+    mark(4)
+    back = all_to_all_equal(y, group)
+    mark(5)
+    out = combine(back, d.tok_row, M, world, H)
     mark(6)
     return out

@@ -175,6 +175,15 @@ W4A16_API int w4a16_moe_forward_noalloc(const void* hidden, int64_t M, int64_t H
 W4A16_API int64_t w4a16_moe_noalloc_max_workspace(void);
 
 /*
+ * Status word of the last w4a16_moe_forward_noalloc call of this shape on the
+ * current device (no reference counterpart): bits of bounded device waits
+ * that ran out, as w4a16_moe_read_status reports them; reading clears them.
+ * Synchronises `stream`.
+ */
+W4A16_API int w4a16_moe_noalloc_read_status(int64_t M, int64_t topk, int64_t E, int64_t H, int64_t I,
+                                            int32_t* status_out, void* stream);
+
+/*
  * Expert-parallel token exchange (no counterpart in the reference, which runs
  * on one GPU; these serve vLLM's expert_map / global_num_experts contract).
  * Rank r of G owns experts [r*E/G, (r+1)*E/G); E % G == 0.
@@ -199,6 +208,23 @@ W4A16_API int w4a16_ep_pack(const void* hidden, int64_t hidden_ld, const void* t
                     int32_t* meta_send, void* stream);
 W4A16_API int w4a16_ep_combine(const void* back, const int32_t* tok_row, int64_t M, int64_t n_ranks,
                     int64_t H, void* out, void* stream);
+
+/*
+ * Fixed-capacity dispatch (no reference counterpart): plan + pack into G
+ * blocks of `capacity` rows (capacity >= M, equal on every rank), so the
+ * exchange is one all-to-all with equal splits and needs no host read of the
+ * counts.  Block r: the tokens routed to rank r in ascending order, then
+ * padding rows whose top-k ids are -1.  Row i of send_rows (row_stride bf16
+ * elements, row_stride >= H + 4*topk, a multiple of 8) = [hidden | top-k ids
+ * int32 | top-k weights fp32 bits | zeros].  send_counts [G]: valid rows per
+ * block; send_tok [G*capacity]: token of each valid row; tok_row [M*G]: row
+ * of (token m, rank r) or -1 (for w4a16_ep_combine on the returned rows).
+ */
+W4A16_API int w4a16_ep_dispatch_fixed(const void* hidden, int64_t hidden_ld, const void* topk_ids,
+                    int ids_is_int64, const float* topk_weights, int64_t M, int64_t topk,
+                    int64_t num_experts, int64_t H, int64_t n_ranks, int64_t capacity,
+                    int64_t row_stride, void* send_rows, int32_t* send_counts, int32_t* send_tok,
+                    int32_t* tok_row, void* stream);
 
 #ifdef __cplusplus
 }

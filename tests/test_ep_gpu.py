@@ -122,6 +122,43 @@ def test_emulated_expert_parallel_layer(ep, world, M):
     assert d < 5e-3, d
 
 
+@pytest.mark.parametrize("world,M", [(4, 600), (8, 64), (2, 3000), (1, 17)])
+def test_emulated_fixed_capacity_layer(ep, world, M):
+    """Fixed-capacity exchange, all ranks' work on one GPU: block r of the send
+    buffer is what rank r receives from this source; its padding rows route
+    nowhere; the combined result equals the all-experts forward."""
+    from kernels import w4a16_moe as K
+    from kernels.synthetic import make_hidden, make_layer, make_routing
+
+    E, H, I, k = 256, 3072, 1024, 10
+    dev = torch.device("cuda")
+    layer = make_layer(E, H, I, seed=0, device="cuda")
+    w1r, s1r = K.repack_weights(layer["w1_q"], layer["w1_s"])
+    w2r, s2r = K.repack_weights(layer["w2_q"], layer["w2_s"])
+    del layer
+    x = make_hidden(M, H, device="cuda")
+    tw, ids = make_routing(M, E, k, device="cuda")
+    full = K.fused_experts_w4a16(x, w1r, w2r, s1r, s2r, tw, ids)
+    cap = M + 5
+    d = ep.dispatch_fixed(x, tw, ids, E, world, cap)
+    rc, _, rs, rt = EO.plan(ids.cpu().numpy(), E, world)
+    np.testing.assert_array_equal(d.counts.cpu().numpy(), rc)
+    backs = []
+    for r in range(world):
+        blk = d.send[r * cap:(r + 1) * cap]
+        xr, idr, wr = ep.unpack_rows(blk, H, k)
+        assert (idr[int(rc[r]):] == -1).all()
+        assert torch.equal(xr[: int(rc[r])], x[torch.as_tensor(rs[int(sum(rc[:r])):int(sum(rc[:r + 1]))],
+                                                              device=dev, dtype=torch.int64)])
+        own = ep.owned_experts(E, world, r)
+        backs.append(K.fused_experts_w4a16(xr, w1r[own.start:own.stop], w2r[own.start:own.stop],
+                                           s1r[own.start:own.stop], s2r[own.start:own.stop], wr, idr,
+                                           expert_map=ep.local_expert_map(E, world, r, dev), global_num_experts=E))
+    out = ep.combine(torch.cat(backs), d.tok_row, M, world, H)
+    dd = ((out.float() - full.float()).norm() / full.float().norm()).item()
+    assert dd < 5e-3, dd
+
+
 def _free_port() -> int:
     with socket.socket(socket.AF_INET, socket.SOCK_STREAM) as s:
         s.bind(("127.0.0.1", 0))

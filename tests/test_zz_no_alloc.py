@@ -66,6 +66,14 @@ def test_noalloc_matches_regular_entry_point(K):
         assert np.isfinite(o).all()
         assert O.rel_frobenius(o, r) <= 1e-2
         assert O.max_abs_err(o, r) <= 1e-2 * float(np.abs(r).max())
+        # no bounded device wait ran out inside the call
+        i64 = ctypes.c_int64
+        lib.w4a16_moe_noalloc_read_status.argtypes = [i64, i64, i64, i64, i64, ctypes.POINTER(ctypes.c_int32),
+                                                      ctypes.c_void_p]
+        status = ctypes.c_int32(-1)
+        assert lib.w4a16_moe_noalloc_read_status(M, ids.shape[1], E, H, I, ctypes.byref(status),
+                                                 torch.cuda.current_stream().cuda_stream) == 0
+        assert status.value == 0
 
 
 def test_noalloc_rejects_oversized_shapes(K):
