@@ -282,6 +282,24 @@ int w4a16_repack(const uint8_t* w_q, const void* scales, int64_t E, int64_t N_ou
   return kOk;
 }
 
+int w4a16_repack_checkpoint(const int32_t* w_packed, const void* scales, int64_t E, int64_t N_out, int64_t K,
+                            int64_t group_size, uint8_t* w_rep, void* s_rep, void* stream) {
+  g_last_error.clear();
+  if (E <= 0 || N_out <= 0 || K <= 0 || !w_packed || !scales || !w_rep || !s_rep)
+    return fail(kInvalidArgument, "w4a16_repack_checkpoint: bad arguments");
+  if (N_out % 16 != 0 || K % 64 != 0)
+    return fail(kUnsupported, "w4a16_repack_checkpoint: need N_out %% 16 == 0 and K %% 64 == 0 (N_out=%lld K=%lld)",
+                (long long)N_out, (long long)K);
+  if (group_size <= 0 || group_size % 32 != 0 || K % group_size != 0)
+    return fail(kUnsupported, "w4a16_repack_checkpoint: group_size=%lld must be a multiple of 32 dividing K=%lld",
+                (long long)group_size, (long long)K);
+  RepackParams p{nullptr, (const uint16_t*)scales, (int)E, (int)N_out, (int)K, (int)group_size,
+                 (uint32_t*)w_rep, (uint16_t*)s_rep, w_packed, 1};
+  cudaError_t err = launch_repack(p, (cudaStream_t)stream);
+  if (err != cudaSuccess) return cuda_fail(err, "w4a16_repack_checkpoint");
+  return kOk;
+}
+
 int64_t w4a16_moe_workspace_size(int64_t M, int64_t topk, int64_t E, int64_t H, int64_t I) {
   if (M < 0 || topk <= 0 || E <= 0 || H <= 0 || I <= 0) return -1;
   return carve(nullptr, M, topk, E, H, I).bytes;

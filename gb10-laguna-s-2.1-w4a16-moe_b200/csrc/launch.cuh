@@ -45,6 +45,8 @@ struct RepackParams {
   int E, N_out, K, G;
   uint32_t* w_rep;          // (E, N_out/16, K/64, 128) words
   uint16_t* s_rep;          // (E, N_out/16, K/64, 32)
+  const int32_t* w_i32t;    // checkpoint form (E, K/8, N_out) int32 instead of w_q (nullable)
+  int scales_t;             // scales given as (E, K/G, N_out)
 };
 cudaError_t launch_repack(const RepackParams& p, cudaStream_t stream);
 

@@ -6,6 +6,9 @@
 // library's kernels read the result, so the layout is ours to choose.
 // Input packing is compressed-tensors / vLLM's: byte j of a row holds element
 // 2j in the low nibble and 2j+1 in the high nibble (stored value = q + 8).
+// The same kernels also read the checkpoint form directly (vLLM create_weights
+// with is_transposed=True): int32 (E, K/8, N_out) with code j of a word at
+// bits 4j, scales (E, K/G, N_out) -- so a load path needs no transpose copy.
 #include <algorithm>
 
 #include "launch.cuh"
@@ -13,6 +16,10 @@
 namespace w4moe {
 
 __device__ __forceinline__ uint32_t code_at(const RepackParams& p, int e, int row, int k) {
+  if (p.w_i32t != nullptr) {  // checkpoint form: (E, K/8, N_out) int32, code k%8 at bits 4*(k%8)
+    const uint32_t word = (uint32_t)p.w_i32t[((size_t)e * (p.K / 8) + (k >> 3)) * p.N_out + row];
+    return (word >> (4 * (k & 7))) & 0xFu;
+  }
   const uint8_t b = p.w_q[((size_t)e * p.N_out + row) * (p.K / 2) + (k >> 1)];
   return (k & 1) ? (b >> 4) : (b & 0xF);
 }
@@ -59,7 +66,8 @@ __global__ void repack_scales_kernel(RepackParams p) {
     const int row = r * kRowTile + g + (which & 1) * 8;
     const int grp32 = c * 2 + (which >> 1);
     const int src_grp = (grp32 * kGroup) / p.G;
-    p.s_rep[idx] = p.scales[((size_t)e * p.N_out + row) * ng + src_grp];
+    p.s_rep[idx] = p.scales_t ? p.scales[((size_t)e * ng + src_grp) * p.N_out + row]
+                              : p.scales[((size_t)e * p.N_out + row) * ng + src_grp];
   }
 }
 

@@ -5,6 +5,8 @@ __all__ = [
     "repack_weights",
     "moe_align_block_size",
     "is_repacked",
+    "repack_checkpoint",
+    "topk_softmax",
 ]
 
 

@@ -108,6 +108,10 @@ def _bind(lib: ctypes.CDLL) -> None:
     lib.w4a16_moe_align_ex.argtypes = [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp]
     lib.w4a16_repack.restype = c_int
     lib.w4a16_repack.argtypes = [c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp]
+    lib.w4a16_topk_softmax.restype = c_int
+    lib.w4a16_topk_softmax.argtypes = [c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp]
+    lib.w4a16_repack_checkpoint.restype = c_int
+    lib.w4a16_repack_checkpoint.argtypes = [c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp]
     lib.w4a16_moe_workspace_size.restype = c_i64
     lib.w4a16_moe_workspace_size.argtypes = [c_i64, c_i64, c_i64, c_i64, c_i64]
     lib.w4a16_moe_forward.restype = c_int
@@ -210,6 +214,62 @@ def repack_weights(
             "w4a16_repack",
         )
     return w_rep, s_rep
+
+
+def repack_checkpoint(w_packed: torch.Tensor, scales: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Library layout straight from vLLM's ``create_weights`` tensors.
+
+    ``w_packed``: ``(E, K_in//8, N_out)`` int32 compressed-tensors
+    ``pack-quantized`` codes (is_transposed=True: 8 codes of one output row
+    per int32 along K, code j at bits 4j); ``scales``: ``(E, K_in//group,
+    N_out)`` bf16.  Equals ``repack_weights(w_packed.transpose(1, 2)
+    .contiguous().view(torch.uint8), scales.transpose(1, 2).contiguous())``
+    (the reference's load path, ``integration/apply.py:100-105``) without the
+    transposed copies.
+    """
+    assert w_packed.ndim == 3 and scales.ndim == 3
+    _require_cuda(w_packed, scales)
+    assert w_packed.dtype == torch.int32, "packed weights must be int32"
+    assert scales.dtype == torch.bfloat16, "scales must be bf16"
+    E, K8, N_out = w_packed.shape
+    K = 8 * K8
+    assert scales.shape[0] == E and scales.shape[2] == N_out
+    num_groups = scales.shape[1]
+    assert num_groups > 0 and K % num_groups == 0
+    group = K // num_groups
+    w_packed = w_packed.contiguous()
+    scales = scales.contiguous()
+    dev = w_packed.device
+    w_rep = torch.empty((E, N_out // _ROW_TILE, K // _CHUNK_K, _CHUNK_BYTES), dtype=torch.uint8, device=dev)
+    s_rep = torch.empty((E, N_out // _ROW_TILE, K // _CHUNK_K, _CHUNK_SCALES), dtype=torch.bfloat16, device=dev)
+    with torch.cuda.device(dev):
+        _check(
+            load_library().w4a16_repack_checkpoint(
+                w_packed.data_ptr(), scales.data_ptr(), E, N_out, K, group,
+                w_rep.data_ptr(), s_rep.data_ptr(), _stream_ptr(dev),
+            ),
+            "w4a16_repack_checkpoint",
+        )
+    return w_rep, s_rep
+
+
+def topk_softmax(logits: torch.Tensor, topk: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Router on the GPU: ``(topk_weights [M, topk] fp32, topk_ids [M, topk]
+    int32)`` = softmax over the top-k of fp32 ``logits [M, E]``, ids in
+    descending logit order -- the reference benchmark's routing
+    (``bench/bench_moe.py:225-231``)."""
+    _require_cuda(logits)
+    assert logits.ndim == 2 and logits.dtype == torch.float32, "logits must be fp32 [M, E]"
+    if logits.stride(1) != 1:
+        logits = logits.contiguous()
+    M, E = logits.shape
+    dev = logits.device
+    w = torch.empty((M, topk), dtype=torch.float32, device=dev)
+    ids = torch.empty((M, topk), dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        _check(load_library().w4a16_topk_softmax(logits.data_ptr(), M, E, logits.stride(0), topk, w.data_ptr(),
+                                                 ids.data_ptr(), _stream_ptr(dev)), "w4a16_topk_softmax")
+    return w, ids
 
 
 def is_repacked(w_q: torch.Tensor) -> bool:

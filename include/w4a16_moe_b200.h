@@ -125,6 +125,29 @@ W4A16_API int w4a16_set_wait_test(int mode);
 W4A16_API int w4a16_repack(const uint8_t* w_q, const void* scales, int64_t E, int64_t N_out, int64_t K,
                  int64_t group_size, uint8_t* w_rep, void* s_rep, void* stream);
 
+/*
+ * Same output as w4a16_repack, read straight from the checkpoint's
+ * compressed-tensors pack-quantized tensors as vLLM's create_weights stores
+ * them (is_transposed=True): w_packed int32 (E, K/8, N_out), code j of a word
+ * at bits 4j (stored value q + 8); scales bf16 (E, K/group, N_out).  Replaces
+ * the transpose(1, 2).contiguous().view(uint8) + repack_weights of the load
+ * path (integration/apply.py:100-105 and kernels/w4a16_moe.py:63-116 in the
+ * reference) with one launch pair and no intermediate copy.
+ */
+W4A16_API int w4a16_repack_checkpoint(const int32_t* w_packed, const void* scales, int64_t E, int64_t N_out,
+                    int64_t K, int64_t group_size, uint8_t* w_rep, void* s_rep, void* stream);
+
+/*
+ * Router: per token, the top-k experts of fp32 logits [M, E] (row stride
+ * logits_ld) in descending logit order (ties: lower id) and the softmax of
+ * those k logits -- the routing the reference benchmarks
+ * (bench/bench_moe.py:225-231: torch.topk then torch.softmax over the k
+ * values).  topk_weights [M, topk] fp32, topk_ids [M, topk] int32;
+ * E <= 1024, topk <= 32.  Logits must be finite.
+ */
+W4A16_API int w4a16_topk_softmax(const float* logits, int64_t M, int64_t E, int64_t logits_ld, int64_t topk,
+                    float* topk_weights, int32_t* topk_ids, void* stream);
+
 /* Bytes of workspace w4a16_moe_forward needs for this shape. */
 W4A16_API int64_t w4a16_moe_workspace_size(int64_t M, int64_t topk, int64_t E, int64_t H, int64_t I);
 

@@ -148,6 +148,23 @@ def test_forward_config0_golden(K, golden_dir, path):
     assert torch.equal(out3, out)
 
 
+@pytest.mark.parametrize("E,N,Kdim,group", [(3, 32, 128, 32), (2, 256, 512, 64), (2, 2048, 3072, 32)])
+def test_repack_checkpoint_bitexact(K, E, N, Kdim, group):
+    """int32 pack-quantized checkpoint tensors (vLLM create_weights form) ->
+    library layout in one launch pair, bit-exact vs pack_int32_along_k +
+    repack_layout of the oracle."""
+    g = np.random.default_rng(E * N + group)
+    codes = g.integers(0, 16, size=(E, N, Kdim), dtype=np.uint8)
+    s = (torch.rand(E, N, Kdim // group, generator=torch.Generator().manual_seed(N)) * 0.015 + 0.005).to(torch.bfloat16)
+    packed = O.pack_int32_along_k(codes)                      # (E, N, K/8) int32
+    w_ckpt = torch.from_numpy(np.ascontiguousarray(packed.transpose(0, 2, 1))).cuda()  # (E, K/8, N)
+    s_ckpt = s.transpose(1, 2).contiguous().cuda()            # (E, K/G, N)
+    wr, sr = K.repack_checkpoint(w_ckpt, s_ckpt)
+    ow, os_ = O.repack_layout(O.int32_pack_to_uint8(packed), _bits(s), group)
+    np.testing.assert_array_equal(wr.cpu().numpy(), ow)
+    np.testing.assert_array_equal(_bits(sr), os_)
+
+
 # ---------------------------------------------------------------------------
 # forward: the 256-expert / top-10 / 3072 x 1024 layer
 # ---------------------------------------------------------------------------
@@ -301,3 +318,44 @@ def test_cuda_graph_capture_and_replay(K, big_layer):
     torch.cuda.synchronize()
     eager = _run(K, big_layer, h2.contiguous(), tw2[:M].contiguous(), ids2[:M].contiguous())
     assert torch.equal(static_out, eager)
+
+
+# ---------------------------------------------------------------------------
+# router (logits -> top-k ids + softmax weights)
+# ---------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("M,E,k", [(1, 256, 10), (257, 256, 10), (4096, 256, 10), (33, 8, 2), (5, 1024, 32)])
+def test_topk_softmax_matches_reference_routing(K, M, E, k):
+    """ids bit-exact with torch.topk on the same seeded logits (the reference's
+    make_routing, bench/bench_moe.py:225-231); weights within 2 ulp of
+    torch.softmax over the k values."""
+    g = torch.Generator().manual_seed(17_000 + M)
+    logits = torch.randn(M, E, generator=g, dtype=torch.float32)
+    vals, ids_ref = torch.topk(logits, k=k, dim=-1)
+    w_ref = torch.softmax(vals, dim=-1)
+    w, ids = K.topk_softmax(logits.cuda(), k)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(ids.cpu().numpy(), ids_ref.to(torch.int32).numpy())
+    wr = w_ref.numpy()
+    ulp = np.spacing(np.abs(wr).astype(np.float32))
+    assert float(np.max(np.abs(w.cpu().numpy() - wr) / ulp)) <= 2.0
+
+
+def test_router_feeds_forward(K, big_layer):
+    """Routing computed on the GPU from logits drives the layer exactly as the
+    reference's host-side routing does."""
+    from kernels.synthetic import make_hidden, make_routing
+
+    M = 3
+    hidden = make_hidden(M, 3072, device="cuda")
+    g = torch.Generator(device="cpu")
+    g.manual_seed(0 + 17_000 + M)  # make_routing's generator
+    logits = torch.randn(M, 256, generator=g, dtype=torch.float32)
+    tw_ref, ids_ref = make_routing(M, 256, 10, device="cuda")
+    tw, ids = K.topk_softmax(logits.cuda(), 10)
+    assert torch.equal(ids, ids_ref)
+    out = _run(K, big_layer, hidden, tw, ids)
+    ref = _run(K, big_layer, hidden, tw_ref, ids_ref)
+    torch.cuda.synchronize()
+    check_close(out, ref.float().cpu().numpy(), None, "router -> forward")
