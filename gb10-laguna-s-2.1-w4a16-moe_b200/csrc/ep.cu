@@ -147,55 +147,83 @@ __global__ void ep_combine_kernel(const __nv_bfloat16* back, const int32_t* tok_
 // top-k weights (fp32 bits) | zero pad], row_stride bf16 elements, so one
 // all-to-all with equal splits moves rows and routing together.
 
-// One CTA per destination rank: ascending-token scan of "routed to rank r".
-__global__ void __launch_bounds__(kEpPlanThreads, 1)
-    ep_plan_fixed_kernel(const void* ids, int is64, int M, int topk, int E, int G, int cap, int32_t* counts,
-                         int32_t* send_tok, int32_t* tok_row) {
-  __shared__ int warp_tot[33];
-  __shared__ int s_base;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, r = blockIdx.x;
-  const int per = E / G;
-  if (tid == 0) s_base = 0;
+// Plan over a (token chunk, destination rank) grid: chunk c of kEpPlanThreads
+// tokens.  Pass 1 counts the chunk's tokens routed to rank r; pass 2 adds the
+// counts of the earlier chunks and scans inside the chunk (ascending tokens).
+__device__ __forceinline__ int ep_routed_to(const void* ids, int is64, int m, int M, int topk, int E, int per,
+                                            int r) {
+  if (m >= M) return 0;
+  for (int t = 0; t < topk; ++t) {
+    const long long e = ep_id(ids, is64, (long long)m * topk + t);
+    if (e >= 0 && e < E && (int)(e / per) == r) return 1;
+  }
+  return 0;
+}
+
+// Block-wide exclusive scan of f (kEpPlanThreads threads); returns the
+// exclusive prefix, *total receives the block sum.
+__device__ __forceinline__ int ep_block_scan(int f, int* warp_tot, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = f;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += u;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
   __syncthreads();
-  for (int m0 = 0; m0 < M; m0 += kEpPlanThreads) {
-    const int m = m0 + tid;
-    int f = 0;
-    if (m < M) {
-      for (int t = 0; t < topk; ++t) {
-        const long long e = ep_id(ids, is64, (long long)m * topk + t);
-        if (e >= 0 && e < E && (int)(e / per) == r) f = 1;
-      }
-    }
-    int incl = f;
+  if (warp == 0) {
+    const int w = warp_tot[lane];
+    int wi = w;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int u = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += u;
+      const int u = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += u;
     }
-    if (lane == 31) warp_tot[warp] = incl;
-    __syncthreads();
-    if (warp == 0) {
-      const int w = warp_tot[lane];
-      int wi = w;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int u = __shfl_up_sync(0xffffffffu, wi, o);
-        if (lane >= o) wi += u;
-      }
-      warp_tot[lane] = wi - w;
-      if (lane == 31) warp_tot[32] = wi;
-    }
-    __syncthreads();
-    const int pos = s_base + warp_tot[warp] + incl - f;
-    if (m < M) {
-      tok_row[(size_t)m * G + r] = f ? r * cap + pos : -1;
-      if (f) send_tok[(size_t)r * cap + pos] = m;
-    }
-    __syncthreads();
-    if (tid == 0) s_base += warp_tot[32];
-    __syncthreads();
+    warp_tot[lane] = wi - w;
+    if (lane == 31) warp_tot[32] = wi;
   }
-  if (tid == 0) counts[r] = s_base;
+  __syncthreads();
+  *total = warp_tot[32];
+  return warp_tot[warp] + incl - f;
+}
+
+__global__ void __launch_bounds__(kEpPlanThreads) ep_plan_fixed_count_kernel(const void* ids, int is64, int M,
+                                                                             int topk, int E, int G,
+                                                                             int32_t* chunk_counts) {
+  __shared__ int warp_tot[33];
+  const int c = blockIdx.x, r = blockIdx.y;
+  const int f = ep_routed_to(ids, is64, c * kEpPlanThreads + threadIdx.x, M, topk, E, E / G, r);
+  int total;
+  ep_block_scan(f, warp_tot, &total);
+  if (threadIdx.x == 0) chunk_counts[(size_t)r * gridDim.x + c] = total;
+}
+
+__global__ void __launch_bounds__(kEpPlanThreads) ep_plan_fixed_scatter_kernel(const void* ids, int is64, int M,
+                                                                               int topk, int E, int G, int cap,
+                                                                               const int32_t* chunk_counts,
+                                                                               int32_t* counts, int32_t* send_tok,
+                                                                               int32_t* tok_row) {
+  __shared__ int warp_tot[33];
+  __shared__ int s_base;
+  const int c = blockIdx.x, r = blockIdx.y, nch = gridDim.x;
+  if (threadIdx.x < 32) {  // counts of the earlier chunks of rank r
+    int b = 0;
+    for (int cc = threadIdx.x; cc < c; cc += 32) b += chunk_counts[(size_t)r * nch + cc];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) b += __shfl_xor_sync(0xffffffffu, b, o);
+    if (threadIdx.x == 0) s_base = b;
+  }
+  const int m = c * kEpPlanThreads + threadIdx.x;
+  const int f = ep_routed_to(ids, is64, m, M, topk, E, E / G, r);
+  int total;
+  const int ex = ep_block_scan(f, warp_tot, &total);  // its __syncthreads also publishes s_base
+  const int pos = s_base + ex;
+  if (m < M) {
+    tok_row[(size_t)m * G + r] = f ? r * cap + pos : -1;
+    if (f) send_tok[(size_t)r * cap + pos] = m;
+  }
+  if (c == nch - 1 && threadIdx.x == 0) counts[r] = s_base + total;
 }
 
 __global__ void ep_pack_fixed_kernel(const __nv_bfloat16* x, long long x_ld, const void* ids, int is64,
@@ -287,9 +315,19 @@ W4A16_API int w4a16_ep_dispatch_fixed(const void* hidden, int64_t hidden_ld, con
   if ((M > 0 && (!hidden || !topk_ids || !topk_weights || !tok_row)) || !send_rows || !send_counts || !send_tok)
     return report_error(kInvalidArgument, "w4a16_ep_dispatch_fixed: null pointer");
   cudaStream_t st = (cudaStream_t)stream;
-  ep_plan_fixed_kernel<<<(int)n_ranks, kEpPlanThreads, 0, st>>>(topk_ids, ids_is_int64, (int)M, (int)topk,
-                                                                 (int)num_experts, (int)n_ranks, (int)capacity,
-                                                                 send_counts, send_tok, tok_row);
+  const int nch = (int)((M + kEpPlanThreads - 1) / kEpPlanThreads);
+  if (nch > 0) {
+    int32_t* chunk_counts = send_counts + n_ranks;  // scratch tail of the counts buffer
+    const dim3 grid(nch, (unsigned)n_ranks);
+    ep_plan_fixed_count_kernel<<<grid, kEpPlanThreads, 0, st>>>(topk_ids, ids_is_int64, (int)M, (int)topk,
+                                                                 (int)num_experts, (int)n_ranks, chunk_counts);
+    ep_plan_fixed_scatter_kernel<<<grid, kEpPlanThreads, 0, st>>>(topk_ids, ids_is_int64, (int)M, (int)topk,
+                                                                   (int)num_experts, (int)n_ranks, (int)capacity,
+                                                                   chunk_counts, send_counts, send_tok, tok_row);
+  } else {
+    cudaError_t e0 = cudaMemsetAsync(send_counts, 0, sizeof(int32_t) * n_ranks, st);
+    if (e0 != cudaSuccess) return report_error(kCudaError, cudaGetErrorString(e0));
+  }
   const long long work = n_ranks * capacity * (row_stride / 8);
   ep_pack_fixed_kernel<<<grid_for(work, 256), 256, 0, st>>>(
       (const __nv_bfloat16*)hidden, hidden_ld, topk_ids, ids_is_int64, topk_weights, (int)topk, (int)H,

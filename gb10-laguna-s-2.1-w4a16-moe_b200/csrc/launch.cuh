@@ -141,6 +141,33 @@ int sliced_plan(SlicedParams& p, int sms, int max_smem);
 cudaError_t launch_sliced(const SlicedParams& p, cudaStream_t stream);
 __host__ __device__ int sliced_w2_start(int c, int A, int P, int G, int chA, int chB, int nrt2);
 
+// ---- decode_split.cu (two-kernel stream-K decode, M <= 4) ----
+constexpr int kSplitMaxM = 4;
+constexpr int kSplitMaxSlots = 64;   // M * topk
+constexpr int kSplitMaxGrid = 320;   // CTAs of 16 warps (sizes the piece buffers)
+
+struct SplitParams {
+  const uint8_t *w13, *s13, *w2, *s2;  // fragment-major weights and scales
+  const __nv_bfloat16* hidden;
+  long long hidden_ld;
+  SlotMap map;
+  int n_tok, topk, M, E, H, I;
+  const float* topk_w;       // [n_tok]
+  __nv_bfloat16* out;        // [M, H]
+  __nv_bfloat16* inter;      // [n_tok, I] intermediate rows (lane-permuted)
+  float* pieces13;           // [kSplitMaxGrid * 16 warps * 2][2 * 16 * Mp]
+  float* pieces2;            // [kSplitMaxGrid * 16 warps * 2][16 * Mp]
+  int32_t* cnt13;            // [n_tok * I / 16] arrivals per w13 pair (zero between calls)
+  int32_t* cnt2;             // [H / 16] arrivals per hidden row tile (zero between calls)
+  int32_t* done13;           // [1] completed w13 pairs (zero between calls)
+  int32_t* done2;            // [1] completed w2 row tiles (zero between calls)
+  int32_t* sched;            // status word at [2]
+  long long* trace;          // diagnostics: CTA 0 timestamps (nullptr normally)
+  int grid, Mp, smem13;      // plan (split_plan)
+};
+int split_plan(SplitParams& p, int sms);
+cudaError_t launch_split(const SplitParams& p, cudaStream_t stream);
+
 // ---- prefill.cu (tcgen05 grouped GEMMs for large M) ----
 struct PrefillParams {
   const uint8_t* w;          // fragment-major weights of this projection

@@ -7,6 +7,7 @@
 // torch.softmax over the k values, fp32).  Ties go to the lower expert id.
 // One warp per token: the logit row is staged in shared memory, k rounds of
 // warp-wide argmax select the experts, lane j < k then holds the j-th value.
+// The weights are computed in double precision and rounded once to fp32.
 #include <math.h>
 
 #include "../../include/w4a16_moe_b200.h"
@@ -56,14 +57,15 @@ __global__ void __launch_bounds__(kRouterWarps * 32) topk_softmax_kernel(const f
       if (lane == 0) row[bi] = -INFINITY;  // taken
       __syncwarp();
     }
-    // softmax over the k selected values (the first is the largest)
+    // softmax over the k selected values (the first is the largest), in
+    // double precision and rounded once: within 1 ulp of the exact value
     const float vmax = __shfl_sync(0xffffffffu, my_v, 0);
-    const float ex = lane < topk ? expf(my_v - vmax) : 0.f;
-    float sum = ex;
+    const double ex = lane < topk ? exp((double)my_v - (double)vmax) : 0.0;
+    double sum = ex;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
     if (lane < topk) {
-      weights[(size_t)m * topk + lane] = ex / sum;
+      weights[(size_t)m * topk + lane] = (float)(ex / sum);
       ids[(size_t)m * topk + lane] = my_i;
     }
     __syncwarp();

@@ -207,7 +207,7 @@ def dispatch_fixed(hidden: torch.Tensor, topk_weights: torch.Tensor, topk_ids: t
     if hidden.stride(1) != 1:
         hidden = hidden.contiguous()
     send = torch.empty((world * capacity, rs), dtype=torch.bfloat16, device=dev)
-    counts = torch.empty(world, dtype=torch.int32, device=dev)
+    counts = torch.empty(world * (1 + (M + 1023) // 1024), dtype=torch.int32, device=dev)
     send_tok = torch.empty(max(world * capacity, 1), dtype=torch.int32, device=dev)
     tok_row = torch.empty(max(M * world, 1), dtype=torch.int32, device=dev)
     with torch.cuda.device(dev):
@@ -218,7 +218,7 @@ def dispatch_fixed(hidden: torch.Tensor, topk_weights: torch.Tensor, topk_ids: t
                                            send_tok.data_ptr(), tok_row.data_ptr(), _K._stream_ptr(dev)),
             "w4a16_ep_dispatch_fixed",
         )
-    return FixedDispatch(send, counts, send_tok, tok_row, capacity)
+    return FixedDispatch(send, counts[:world], send_tok, tok_row, capacity)
 
 
 def unpack_rows(rows: torch.Tensor, H: int, topk: int):

@@ -185,7 +185,7 @@ def _run(K, layer, hidden, tw, ids, **kw):
     return K.fused_experts_w4a16(hidden, layer["w1r"], layer["w2r"], layer["s1r"], layer["s2r"], tw, ids, **kw)
 
 
-@pytest.fixture(params=["auto", "general", "prefill", "direct", "sliced", "staged"])
+@pytest.fixture(params=["auto", "general", "prefill", "direct", "sliced", "staged", "split"])
 def path(request, K):
     K.set_path(request.param)
     yield request.param
@@ -328,8 +328,9 @@ def test_cuda_graph_capture_and_replay(K, big_layer):
 @pytest.mark.parametrize("M,E,k", [(1, 256, 10), (257, 256, 10), (4096, 256, 10), (33, 8, 2), (5, 1024, 32)])
 def test_topk_softmax_matches_reference_routing(K, M, E, k):
     """ids bit-exact with torch.topk on the same seeded logits (the reference's
-    make_routing, bench/bench_moe.py:225-231); weights within 2 ulp of
-    torch.softmax over the k values."""
+    make_routing, bench/bench_moe.py:225-231); weights within 1 ulp of the
+    exact softmax of the k values (float64) and within 8 ulp of torch's CPU
+    softmax (whose own vectorised exp and summation order are off by a few ulp)."""
     g = torch.Generator().manual_seed(17_000 + M)
     logits = torch.randn(M, E, generator=g, dtype=torch.float32)
     vals, ids_ref = torch.topk(logits, k=k, dim=-1)
@@ -337,9 +338,14 @@ def test_topk_softmax_matches_reference_routing(K, M, E, k):
     w, ids = K.topk_softmax(logits.cuda(), k)
     torch.cuda.synchronize()
     np.testing.assert_array_equal(ids.cpu().numpy(), ids_ref.to(torch.int32).numpy())
+    wg = w.cpu().numpy()
     wr = w_ref.numpy()
-    ulp = np.spacing(np.abs(wr).astype(np.float32))
-    assert float(np.max(np.abs(w.cpu().numpy() - wr) / ulp)) <= 2.0
+    v64 = vals.double().numpy()
+    e64 = np.exp(v64 - v64[:, :1])
+    exact = e64 / e64.sum(axis=1, keepdims=True)
+    ulp = np.spacing(np.abs(wr).astype(np.float32)).astype(np.float64)
+    assert float(np.max(np.abs(wg - exact) / ulp)) <= 1.0
+    assert float(np.max(np.abs(wg - wr) / ulp)) <= 8.0
 
 
 def test_router_feeds_forward(K, big_layer):

@@ -1,5 +1,5 @@
-"""GPU parity of the expert-sliced decode kernel (M <= 4 tokens, M*topk <= 64
-slots) against the CPU oracle, through the C ABI, on the 256-expert / top-10
+"""GPU parity of the small-batch decode kernels (M <= 4 tokens, M*topk <= 64
+slots: expert-sliced and two-kernel stream-K) against the CPU oracle, through the C ABI, on the 256-expert / top-10
 / 3072 x 1024 layer and on edge cases of its routing (duplicate experts in a
 token, int64 ids, strided rows, topk = 1, a shard with no local slot)."""
 
@@ -13,9 +13,11 @@ from test_gpu_parity import K, big_layer, check_close, oracle_for  # noqa: F401 
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture
-def sliced(K):  # noqa: F811
-    K.set_path("sliced")
+@pytest.fixture(params=["sliced", "split"])
+def sliced(K, request):  # noqa: F811
+    """Both small-batch decode kernels: the expert-sliced one and the
+    two-kernel stream-K one."""
+    K.set_path(request.param)
     yield K
     K.set_path("auto")
 
