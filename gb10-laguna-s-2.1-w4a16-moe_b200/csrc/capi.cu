@@ -86,10 +86,7 @@ constexpr int64_t kMaxAlignBlock = 128;
 
 struct Workspace {
   int32_t *counts, *offsets, *active, *num_active, *num_post, *tok_valid;
-  int32_t *sorted, *expert_ids, *counters, *ready, *sched, *align_bar, *readers, *pflag;
-  float* pieces;
-  int32_t *cnt13, *cnt2;
-  float *pieces13, *pieces2;
+  int32_t *sorted, *expert_ids, *counters, *ready, *sched, *align_bar;
   __nv_bfloat16* inter;
   float* partial;
   int64_t bytes;
@@ -111,10 +108,6 @@ Workspace carve(char* base, int64_t M, int64_t topk, int64_t E, int64_t H, int64
   w.ready = (int32_t*)take(4 * E);
   w.sched = (int32_t*)take(4 * 4);
   w.align_bar = (int32_t*)take(4 * 4);
-  w.readers = (int32_t*)take(4 * E);
-  w.pflag = (int32_t*)take(4 * kSlicedMaxGrid);
-  w.cnt13 = (int32_t*)take(M <= kSplitMaxM ? 4 * n_tok * (I / 16) : 0);
-  w.cnt2 = (int32_t*)take(M <= kSplitMaxM ? 4 * (H / 16 + 2) : 0);  // + done13, done2
   w.counts = (int32_t*)take(4 * E);
   w.offsets = (int32_t*)take(4 * (E + 1));
   w.active = (int32_t*)take(4 * E);
@@ -125,12 +118,6 @@ Workspace carve(char* base, int64_t M, int64_t topk, int64_t E, int64_t H, int64
   w.expert_ids = (int32_t*)take(4 * P);
   w.inter = (__nv_bfloat16*)take(2 * n_tok * I);
   w.partial = (float*)take(4 * n_tok * H);
-  w.pieces = (float*)take(M <= kSlicedMaxM ? 4 * 16 * M * kSlicedMaxGrid : 0);
-  {
-    const int64_t Mp = M <= 2 ? 2 : 4, warps2 = (int64_t)kSplitMaxGrid * 16 * 2;
-    w.pieces13 = (float*)take(M <= kSplitMaxM ? 4 * warps2 * 32 * Mp : 0);
-    w.pieces2 = (float*)take(M <= kSplitMaxM ? 4 * warps2 * 16 * Mp : 0);
-  }
   w.bytes = off;
   return w;
 }
@@ -160,10 +147,8 @@ int w4a16_version(void) { return 100; }
 
 int w4a16_set_path(int path) {
   g_last_error.clear();
-  if (path < 0 || path > 6)
-    return fail(kInvalidArgument,
-                "w4a16_set_path: 0 = auto, 1 = general, 2 = tensor-core prefill, 3 = direct-streaming decode, "
-                "4 = expert-sliced decode, 5 = staged decode, 6 = two-kernel stream-K decode");
+  if (path < 0 || path > 2)
+    return fail(kInvalidArgument, "w4a16_set_path: 0 = auto, 1 = general, 2 = tensor-core prefill");
   g_force_general = path;
   return kOk;
 }
@@ -355,90 +340,8 @@ int w4a16_moe_forward(const void* hidden, int64_t M, int64_t H, int64_t hidden_l
   const SlotMap map{topk_ids, ids_is_int64 ? 1 : 0, expert_map,
                     (int)(expert_map ? global_num_experts : E), (int)E};
 
-  // Smallest M: the expert-sliced fused kernel.
-  if (g_force_general == 4 && ((uintptr_t)hidden & 15) == 0 && (hidden_ld & 7) == 0 && M <= kSlicedMaxM &&
-      n_tok <= kSlicedMaxSlots) {
-    SlicedParams sp{};
-    sp.w13 = (const uint8_t*)w13_rep;
-    sp.s13 = (const uint8_t*)s13_rep;
-    sp.w2 = (const uint8_t*)w2_rep;
-    sp.s2 = (const uint8_t*)s2_rep;
-    sp.hidden = (const __nv_bfloat16*)hidden;
-    sp.hidden_ld = hidden_ld;
-    sp.map = map;
-    sp.n_tok = (int)n_tok;
-    sp.topk = (int)topk;
-    sp.M = (int)M;
-    sp.E = (int)E;
-    sp.H = (int)H;
-    sp.I = (int)I;
-    sp.topk_w = topk_weights;
-    sp.out = (__nv_bfloat16*)out;
-    sp.inter = ws.inter;
-    sp.ready = ws.ready;
-    sp.readers = ws.readers;
-    sp.pflag = ws.pflag;
-    sp.pieces = ws.pieces;
-    sp.sched = ws.sched;
-#ifdef W4A16_DIAGNOSTICS
-    if (const char* tr = getenv("W4A16_SLICED_TRACE")) sp.trace = (long long*)strtoull(tr, nullptr, 0);
-    if (const char* tc = getenv("W4A16_SLICED_TRACE_CTA")) sp.trace_cta = atoi(tc);
-#endif
-    if (sliced_plan(sp, sm_count(), max_smem_optin() - 1024)) {
-      mark_stage(0, st);
-      mark_stage(1, st);
-      cudaError_t err = launch_sliced(sp, st);
-      if (err != cudaSuccess) return cuda_fail(err, "w4a16_moe_forward/decode_sliced");
-      mark_stage(2, st);
-      mark_stage(3, st);
-      return kOk;
-    }
-  }
-
-  // Smallest M: two-kernel stream-K decode.
-  if (g_force_general == 6 && ((uintptr_t)hidden & 15) == 0 && (hidden_ld & 7) == 0 && M <= kSplitMaxM &&
-      n_tok <= kSplitMaxSlots) {
-    SplitParams sp{};
-    sp.w13 = (const uint8_t*)w13_rep;
-    sp.s13 = (const uint8_t*)s13_rep;
-    sp.w2 = (const uint8_t*)w2_rep;
-    sp.s2 = (const uint8_t*)s2_rep;
-    sp.hidden = (const __nv_bfloat16*)hidden;
-    sp.hidden_ld = hidden_ld;
-    sp.map = map;
-    sp.n_tok = (int)n_tok;
-    sp.topk = (int)topk;
-    sp.M = (int)M;
-    sp.E = (int)E;
-    sp.H = (int)H;
-    sp.I = (int)I;
-    sp.topk_w = topk_weights;
-    sp.out = (__nv_bfloat16*)out;
-    sp.inter = ws.inter;
-    sp.pieces13 = ws.pieces13;
-    sp.pieces2 = ws.pieces2;
-    sp.cnt13 = ws.cnt13;
-    sp.cnt2 = ws.cnt2;
-    sp.done13 = ws.cnt2 + H / 16;
-    sp.done2 = ws.cnt2 + H / 16 + 1;
-    sp.sched = ws.sched;
-#ifdef W4A16_DIAGNOSTICS
-    if (const char* tr = getenv("W4A16_SPLIT_TRACE")) sp.trace = (long long*)strtoull(tr, nullptr, 0);
-#endif
-    if (split_plan(sp, sm_count())) {
-      mark_stage(0, st);
-      mark_stage(1, st);
-      cudaError_t err = launch_split(sp, st);
-      if (err != cudaSuccess) return cuda_fail(err, "w4a16_moe_forward/decode_split");
-      mark_stage(2, st);
-      mark_stage(3, st);
-      return kOk;
-    }
-  }
-
   // Small M: one fused persistent kernel (routing + w13 + w2 + top-k sum).
-  if ((g_force_general == 0 || g_force_general == 3 || g_force_general == 5) && ((uintptr_t)hidden & 15) == 0 &&
-      (hidden_ld & 7) == 0) {
+  if (g_force_general == 0 && ((uintptr_t)hidden & 15) == 0 && (hidden_ld & 7) == 0) {
     DecodeParams dp{};
     dp.w13 = (const uint8_t*)w13_rep;
     dp.s13 = (const uint8_t*)s13_rep;
@@ -468,21 +371,7 @@ int w4a16_moe_forward(const void* hidden, int64_t M, int64_t H, int64_t hidden_l
     if (decode_plan(dp, sm_count(), max_smem_optin() - 1024)) {
       mark_stage(0, st);
       mark_stage(1, st);
-#ifdef W4A16_DIAGNOSTICS
-      static const bool staged_only = getenv("W4A16_DECODE_STAGED") != nullptr;  // A/B comparisons
-      static const int direct_min_m = [] {
-        const char* e = getenv("W4A16_DECODE_DIRECT_MIN_M");
-        return e ? atoi(e) : 2;
-      }();
-#else
-      constexpr bool staged_only = false;
-      // the staged kernel measured at least as fast at every M (B200,
-      // E=256 top-10 3072x1024), so the direct kernel runs only on request
-      constexpr int direct_min_m = 1 << 30;
-#endif
-      dp.direct_min_m = g_force_general == 3 ? 1 : direct_min_m;
-      cudaError_t err = (!staged_only && decode_direct_ok(dp, max_smem_optin() - 1024)) ? launch_decode_direct(dp, st)
-                                                                                         : launch_decode(dp, st);
+      cudaError_t err = launch_decode(dp, st);
       if (err != cudaSuccess) return cuda_fail(err, "w4a16_moe_forward/decode");
       mark_stage(2, st);
       mark_stage(3, st);

@@ -102,71 +102,9 @@ struct DecodeParams {
   // plan (decode_plan); the stage geometry is derived per CTA on the device
   int NG, RP, R2, n_red, red_offset, ring_offset, ring_bytes, smem_bytes, grid;
   int ring_div;              // stages are sized to ring_bytes / ring_div
-  int direct_min_m;          // smallest M sent to the direct-streaming kernel
   int geo[kDecGeoRows][4];   // per reserved row count: ncA, ncB, stage bytes, stages
 };
 int decode_plan(DecodeParams& p, int sms, int max_smem);
-// decode_direct.cu: per-warp weight streaming for <= ~1.5 slots per expert (NG == 1)
-bool decode_direct_ok(const DecodeParams& p, int max_smem);
-cudaError_t launch_decode_direct(const DecodeParams& p, cudaStream_t stream);
-
-// ---- decode_sliced.cu (expert-sliced fused layer, M <= 4) ----
-constexpr int kSlicedMaxM = 4;
-constexpr int kSlicedMaxSlots = 64;    // M * topk
-constexpr int kSlicedMaxPieces = 8;    // fp32 row-tile pieces one CTA may add
-constexpr int kSlicedMaxGrid = 1024;   // CTAs (piece flags in the workspace)
-
-struct SlicedParams {
-  const uint8_t *w13, *s13, *w2, *s2;  // fragment-major weights and scales
-  const __nv_bfloat16* hidden;
-  long long hidden_ld;
-  SlotMap map;
-  int n_tok, topk, M, E, H, I;
-  const float* topk_w;       // [n_tok]
-  __nv_bfloat16* out;        // [M, H]
-  __nv_bfloat16* inter;      // [n_tok, I] intermediate rows, expert-sorted, lane-permuted
-  int32_t* ready;            // [E] published w13 pairs per expert (zero between calls)
-  int32_t* readers;          // [E] CTAs done polling ready[e] (zero between calls)
-  int32_t* pflag;            // [grid] row-tile piece published (zero between calls)
-  float* pieces;             // [grid, M, 16] fp32 row-tile pieces
-  int32_t* sched;            // status word at [2]
-  long long* trace;          // optional pipeline timestamps of CTA trace_cta (diagnostics)
-  int trace_cta;
-  // plan (sliced_plan)
-  int grid, smem_bytes, Mp, T2, maxT, lag, nr_cap;
-  int off_x, off_inter, off_red, off_oacc, off_pc, off_table, off_rounds, off_ring, ring_bytes;
-  int n_slots, slot_bytes, max_stages, max_rounds;
-};
-int sliced_plan(SlicedParams& p, int sms, int max_smem);
-cudaError_t launch_sliced(const SlicedParams& p, cudaStream_t stream);
-__host__ __device__ int sliced_w2_start(int c, int A, int P, int G, int chA, int chB, int nrt2);
-
-// ---- decode_split.cu (two-kernel stream-K decode, M <= 4) ----
-constexpr int kSplitMaxM = 4;
-constexpr int kSplitMaxSlots = 64;   // M * topk
-constexpr int kSplitMaxGrid = 320;   // CTAs of 16 warps (sizes the piece buffers)
-
-struct SplitParams {
-  const uint8_t *w13, *s13, *w2, *s2;  // fragment-major weights and scales
-  const __nv_bfloat16* hidden;
-  long long hidden_ld;
-  SlotMap map;
-  int n_tok, topk, M, E, H, I;
-  const float* topk_w;       // [n_tok]
-  __nv_bfloat16* out;        // [M, H]
-  __nv_bfloat16* inter;      // [n_tok, I] intermediate rows (lane-permuted)
-  float* pieces13;           // [kSplitMaxGrid * 16 warps * 2][2 * 16 * Mp]
-  float* pieces2;            // [kSplitMaxGrid * 16 warps * 2][16 * Mp]
-  int32_t* cnt13;            // [n_tok * I / 16] arrivals per w13 pair (zero between calls)
-  int32_t* cnt2;             // [H / 16] arrivals per hidden row tile (zero between calls)
-  int32_t* done13;           // [1] completed w13 pairs (zero between calls)
-  int32_t* done2;            // [1] completed w2 row tiles (zero between calls)
-  int32_t* sched;            // status word at [2]
-  long long* trace;          // diagnostics: CTA 0 timestamps (nullptr normally)
-  int grid, Mp, smem13;      // plan (split_plan)
-};
-int split_plan(SplitParams& p, int sms);
-cudaError_t launch_split(const SplitParams& p, cudaStream_t stream);
 
 // ---- prefill.cu (tcgen05 grouped GEMMs for large M) ----
 struct PrefillParams {

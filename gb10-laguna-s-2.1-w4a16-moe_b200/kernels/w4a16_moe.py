@@ -383,14 +383,10 @@ def set_stage_events(events: list | None) -> None:
 
 def set_path(path: str) -> None:
     """Select the forward implementation for the calling thread: ``"auto"``
-    (fused persistent kernel for small M, tensor-core kernels otherwise),
-    ``"general"`` (multi-kernel CUDA-core path), ``"prefill"`` (the
-    tensor-core path at any M), ``"direct"`` (the direct-streaming decode
-    kernel wherever it applies, the staged one otherwise), ``"sliced"`` (the
-    expert-sliced decode kernel, M <= 4), ``"staged"`` (the staged decode
-    kernel even where a faster one applies) or ``"split"`` (the two-kernel
-    stream-K decode, M <= 4)."""
-    codes = {"auto": 0, "general": 1, "prefill": 2, "direct": 3, "sliced": 4, "staged": 5, "split": 6}
+    (fused persistent decode kernel for small M, tensor-core kernels
+    otherwise), ``"general"`` (multi-kernel CUDA-core path) or ``"prefill"``
+    (the tensor-core path at any M)."""
+    codes = {"auto": 0, "general": 1, "prefill": 2}
     _check(load_library().w4a16_set_path(codes[path]), "w4a16_set_path")
 
 

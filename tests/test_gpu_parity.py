@@ -185,7 +185,7 @@ def _run(K, layer, hidden, tw, ids, **kw):
     return K.fused_experts_w4a16(hidden, layer["w1r"], layer["w2r"], layer["s1r"], layer["s2r"], tw, ids, **kw)
 
 
-@pytest.fixture(params=["auto", "general", "prefill", "direct", "sliced", "staged", "split"])
+@pytest.fixture(params=["auto", "general", "prefill"])
 def path(request, K):
     K.set_path(request.param)
     yield request.param
