@@ -5,7 +5,8 @@ Bars: routing outputs bit-exact; MoE output within
 relative Frobenius error 1e-2 of the fp32 reference everywhere, and max-abs
 2e-2 at configuration 0.  At the 3072-wide layer |out| reaches ~28, where bf16
 output rounding alone exceeds 2e-2, so there the max-abs bar is taken relative
-to max|ref| (<= 1e-2) and reported.
+to max|ref| (<= 1e-2), and at most 1 element in 1000 may lie outside
+2e-2 + half a bf16 ulp of the reference value.
 """
 
 from __future__ import annotations
@@ -21,6 +22,8 @@ pytestmark = pytest.mark.gpu
 REL_FROB_TOL = 1e-2
 MAX_ABS_TOL_CFG0 = 2e-2
 MAX_ABS_REL_TOL = 1e-2
+# elements outside 2e-2 + half a bf16 ulp of the reference: at most 1 in 1000
+OUTSIDE_FRAC_TOL = 1e-3
 
 
 @pytest.fixture(scope="module")
@@ -63,9 +66,14 @@ def check_close(out, ref, max_abs_tol=None, what=""):
     rf = O.rel_frobenius(o, ref)
     ma = O.max_abs_err(o, ref)
     scale = float(np.max(np.abs(ref))) + 1e-12
-    print(f"[{what}] rel_frob={rf:.3e} max_abs={ma:.3e} max_abs/max|ref|={ma / scale:.3e} max|ref|={scale:.2f}")
+    # third form: elements outside max-abs 2e-2 widened by the bf16 rounding of the output
+    outside = int(np.count_nonzero(np.abs(o - ref) > 2e-2 + O.bf16_half_ulp(ref)))
+    frac_out = outside / max(o.size, 1)
+    print(f"[{what}] rel_frob={rf:.3e} max_abs={ma:.3e} max_abs/max|ref|={ma / scale:.3e} max|ref|={scale:.2f} "
+          f"outside(2e-2+ulp/2)={outside}/{o.size}")
     assert np.isfinite(o).all()
     assert rf <= REL_FROB_TOL, (what, rf)
+    assert frac_out <= OUTSIDE_FRAC_TOL, (what, outside, o.size)
     if max_abs_tol is not None:
         assert ma <= max_abs_tol, (what, ma)
     else:
@@ -218,6 +226,39 @@ def test_forward_prefill_token_subset(K, big_layer, M):
     toks = np.random.default_rng(M).choice(M, size=24, replace=False)
     ref = oracle_for(hidden, big_layer, tw, ids, tokens=toks)
     check_close(out[torch.as_tensor(toks, device="cuda")], ref, None, f"M={M} (24 tokens)")
+
+
+def test_forward_prefill_m1024_all_rows(K, big_layer):
+    """Every row of the M=1024 output (the tensor-core path) against the
+    oracle (each routed expert is dequantised once on the host)."""
+    from kernels.synthetic import make_hidden, make_routing
+
+    M = 1024
+    hidden = make_hidden(M, 3072, device="cuda")
+    tw, ids = make_routing(M, 256, 10, device="cuda")
+    out = _run(K, big_layer, hidden, tw, ids)
+    torch.cuda.synchronize()
+    check_close(out, oracle_for(hidden, big_layer, tw, ids), None, "M=1024 all rows")
+
+
+def test_apply_router_weight_on_input_and_inplace(K, big_layer):
+    """vLLM apply() keywords: topk == 1 with the router weight applied to the
+    input rows; inplace writes the result into hidden (and returns it)."""
+    from kernels.synthetic import make_hidden, make_routing
+
+    M = 8
+    hidden = make_hidden(M, 3072, device="cuda")
+    tw, ids = make_routing(M, 256, 1, device="cuda")
+    out = _run(K, big_layer, hidden, tw, ids, apply_router_weight_on_input=True)
+    torch.cuda.synchronize()
+    scaled = (hidden.float() * tw.float()).to(torch.bfloat16)
+    check_close(out, oracle_for(scaled, big_layer, torch.ones_like(tw), ids), None, "router weight on input")
+    ref = _run(K, big_layer, hidden, tw, ids)
+    h2 = hidden.clone()
+    ret = _run(K, big_layer, h2, tw, ids, inplace=True)
+    torch.cuda.synchronize()
+    assert ret.data_ptr() == h2.data_ptr()
+    assert torch.equal(h2, ref)
 
 
 def test_deterministic_and_token_permutation(K, big_layer):
