@@ -56,7 +56,20 @@ def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
 
 
 def round_bf16(x: np.ndarray) -> np.ndarray:
-    return bf16_bits_to_f32(f32_to_bf16_bits(x))
+    """fp32 -> nearest-even bf16 value, kept as fp32 (same result as
+    ``bf16_bits_to_f32(f32_to_bf16_bits(x))``, in 32-bit arithmetic: for
+    every non-NaN input the sum below stays under 2**32)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    u = x.view(np.uint32)
+    r = (u >> 16) & np.uint32(1)
+    r += np.uint32(0x7FFF)
+    r += u
+    r &= np.uint32(0xFFFF0000)
+    out = r.view(np.float32)
+    nan = np.isnan(x)
+    if nan.any():
+        out[nan] = np.float32(np.nan)
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -167,7 +180,8 @@ def silu(x: np.ndarray) -> np.ndarray:
 def moe_reference(hidden: np.ndarray, w1_q: np.ndarray, w1_s: np.ndarray, w2_q: np.ndarray,
                   w2_s: np.ndarray, topk_weights: np.ndarray, topk_ids: np.ndarray,
                   group_size: int = 32, expert_map: np.ndarray | None = None,
-                  round_weights_to_bf16: bool = False) -> np.ndarray:
+                  round_weights_to_bf16: bool = False,
+                  round_intermediate_to_bf16: bool = False) -> np.ndarray:
     """fp32 per-expert reference of the fused MoE (bench/bench_moe.py:277-303).
 
     hidden: [M, H] fp32 values (already bf16-representable).
@@ -175,9 +189,22 @@ def moe_reference(hidden: np.ndarray, w1_q: np.ndarray, w1_s: np.ndarray, w2_q: 
     w2_s (E, H, I/g).  Returns fp32 [M, H]:
     out[m] = sum_t w[m,t] * W2_e(silu(W_gate,e x) * W_up,e x).
     With ``expert_map`` ids are global and mapped to local experts; -1 skips.
+    ``round_weights_to_bf16`` rounds each dequantised weight to bf16 (the
+    reference's ``dequant_int4_w4a16``, bench/bench_moe.py:119);
+    ``round_intermediate_to_bf16`` rounds silu(gate)*up to bf16 before the w2
+    product (the bf16 intermediate cache of vLLM's fused_experts and of the
+    reference's kernel, kernels/w4a16_moe.py).
     """
+    return moe_reference_variants(hidden, w1_q, w1_s, w2_q, w2_s, topk_weights, topk_ids, group_size,
+                                  expert_map, [(round_weights_to_bf16, round_intermediate_to_bf16)])[0]
+
+
+def moe_reference_variants(hidden, w1_q, w1_s, w2_q, w2_s, topk_weights, topk_ids, group_size=32,
+                           expert_map=None, variants=((False, False),)):
+    """:func:`moe_reference` for several (round_weights, round_intermediate)
+    numerics at once, sharing the per-expert dequantisation."""
     M, H = hidden.shape
-    out = np.zeros((M, H), dtype=np.float32)
+    outs = [np.zeros((M, H), dtype=np.float32) for _ in variants]
     ids = np.asarray(topk_ids).astype(np.int64)
     if expert_map is not None:
         emap = np.asarray(expert_map).astype(np.int64)
@@ -189,14 +216,21 @@ def moe_reference(hidden: np.ndarray, w1_q: np.ndarray, w1_s: np.ndarray, w2_q: 
         tok, slot = np.nonzero(ids == e)
         if tok.size == 0:
             continue
-        w1 = dequant(w1_q[e], w1_s[e], group_size, round_weights_to_bf16)
-        w2 = dequant(w2_q[e], w2_s[e], group_size, round_weights_to_bf16)
-        y = h[tok] @ w1.T
-        d = y.shape[-1] // 2
-        y = silu(y[:, :d]) * y[:, d:]
-        y = y @ w2.T
-        np.add.at(out, tok, y * tw[tok, slot][:, None])
-    return out
+        w1x = dequant(w1_q[e], w1_s[e], group_size, False)
+        w2x = dequant(w2_q[e], w2_s[e], group_size, False)
+        w1r = w2r = None
+        for out, (rw, ri) in zip(outs, variants):
+            if rw and w1r is None:
+                w1r, w2r = round_bf16(w1x), round_bf16(w2x)
+            w1, w2 = (w1r, w2r) if rw else (w1x, w2x)
+            y = h[tok] @ w1.T
+            d = y.shape[-1] // 2
+            y = silu(y[:, :d]) * y[:, d:]
+            if ri:
+                y = round_bf16(y)
+            y = y @ w2.T
+            np.add.at(out, tok, y * tw[tok, slot][:, None])
+    return outs
 
 
 def weight_bytes_for_experts(n_experts: int, K: int, N: int, group_size: int) -> int:

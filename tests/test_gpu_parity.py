@@ -22,8 +22,17 @@ pytestmark = pytest.mark.gpu
 REL_FROB_TOL = 1e-2
 MAX_ABS_TOL_CFG0 = 2e-2
 MAX_ABS_REL_TOL = 1e-2
-# elements outside 2e-2 + half a bf16 ulp of the reference: at most 1 in 1000
-OUTSIDE_FRAC_TOL = 1e-3
+# third form: elements with |out - ref_k| > 2e-2 + half a bf16 ulp of ref_k,
+# where ref_k is the oracle with the kernel's roundings (bf16 intermediate
+# between w13 and w2, as in vLLM and the reference kernel; bf16 (q - 8) * s
+# weights on the paths that use them).  Against the pure fp32 oracle the count
+# is not meaningful at this layer: |out| reaches ~70 and the bf16 intermediate
+# alone moves outputs by more than 2e-2.  The decode and general paths have
+# none outside; the tcgen05 prefill path accumulates in the tensor pipe, whose
+# fp32 sums differ slightly from sequential fp32 and flip an occasional bf16
+# intermediate (measured 0.45-0.75 % of elements at M = 1..16384).
+OUTSIDE_FRAC_TOL = 0.0
+PREFILL_OUTSIDE_FRAC_TOL = 1e-2
 
 
 @pytest.fixture(scope="module")
@@ -40,10 +49,25 @@ def _bits(t: torch.Tensor) -> np.ndarray:
     return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
 
 
-def oracle_for(hidden, layer, tw, ids, tokens=None, expert_map=None):
+def weights_rounded(path, M, topk, E):
+    """Whether the library's path for this shape multiplies bf16((q - 8) * s)
+    (the reference's dequantised weight) or keeps (q - 8) exact and applies the
+    scale to the fp32 partial: only the fused decode kernel with NG == 1 does
+    the latter (csrc/decode.cu decode_plan: NG == 1 iff slots per active
+    expert <= 1.5; csrc/capi.cu: the fused decode kernel runs for path "auto"
+    and M * topk <= 4096).  The general and prefill paths always round."""
+    n = M * topk
+    return not (path == "auto" and 0 < n <= 4096 and n / min(n, E) <= 1.5)
+
+
+def oracle_for(hidden, layer, tw, ids, tokens=None, expert_map=None, path="auto"):
     """fp32 oracle on the experts the selected tokens use (weights copied from
-    the device, so both sides read identical bytes)."""
+    the device, so both sides read identical bytes).  Returns (ref, ref_k):
+    ref is the fp32 reference (exact weights, fp32 intermediate), ref_k the
+    same computation with the kernel's roundings (bf16 intermediate, and the
+    bf16 weights of ``weights_rounded``) for the element-wise count."""
     x = hidden.float().cpu().numpy()
+    M_full, topk = ids.shape
     ids_c = ids.cpu().numpy().astype(np.int64)
     tw_c = tw.float().cpu().numpy()
     if tokens is not None:
@@ -58,22 +82,42 @@ def oracle_for(hidden, layer, tw, ids, tokens=None, expert_map=None):
     w2 = layer["w2_q"][sel].cpu().numpy()
     s2 = _bits(layer["w2_s"][sel])
     local = np.where(ids_c >= 0, np.searchsorted(used, np.maximum(ids_c, 0)), -1)
-    return O.moe_reference(x, w1, s1, w2, s2, tw_c, local, 32)
+    rw = weights_rounded(path, M_full, topk, layer["w1_q"].shape[0])
+    ref, ref_k = O.moe_reference_variants(x, w1, s1, w2, s2, tw_c, local, 32,
+                                          variants=[(False, False), (rw, True)])
+    return OracleOut(ref, ref_k)
 
 
-def check_close(out, ref, max_abs_tol=None, what=""):
+class OracleOut(np.ndarray):
+    """The fp32 reference array, carrying the kernel-numerics variant as
+    ``.k``; arrays derived from it (slices, results) do not carry it."""
+
+    def __new__(cls, ref, ref_k):
+        obj = np.asarray(ref).view(cls)
+        obj.k = ref_k
+        return obj
+
+    def __array_finalize__(self, obj):
+        self.k = None
+
+
+def check_close(out, ref, max_abs_tol=None, what="", outside_tol=None):
     o = out.float().cpu().numpy()
+    ref_k = getattr(ref, "k", None)
+    ref = np.asarray(ref)
     rf = O.rel_frobenius(o, ref)
     ma = O.max_abs_err(o, ref)
     scale = float(np.max(np.abs(ref))) + 1e-12
-    # third form: elements outside max-abs 2e-2 widened by the bf16 rounding of the output
-    outside = int(np.count_nonzero(np.abs(o - ref) > 2e-2 + O.bf16_half_ulp(ref)))
+    # third form, against the oracle with the kernel's roundings where known
+    rk = ref if ref_k is None else ref_k
+    outside = int(np.count_nonzero(np.abs(o - rk) > 2e-2 + O.bf16_half_ulp(rk)))
     frac_out = outside / max(o.size, 1)
     print(f"[{what}] rel_frob={rf:.3e} max_abs={ma:.3e} max_abs/max|ref|={ma / scale:.3e} max|ref|={scale:.2f} "
-          f"outside(2e-2+ulp/2)={outside}/{o.size}")
+          f"outside(2e-2+ulp/2{'' if ref_k is None else ', kernel numerics'})={outside}/{o.size} "
+          f"frac={frac_out:.2e}")
     assert np.isfinite(o).all()
     assert rf <= REL_FROB_TOL, (what, rf)
-    assert frac_out <= OUTSIDE_FRAC_TOL, (what, outside, o.size)
+    assert frac_out <= (OUTSIDE_FRAC_TOL if outside_tol is None else outside_tol), (what, outside, o.size)
     if max_abs_tol is not None:
         assert ma <= max_abs_tol, (what, ma)
     else:
@@ -209,8 +253,9 @@ def test_forward_decode_configs(K, big_layer, M, path):
     out = _run(K, big_layer, hidden, tw, ids)
     torch.cuda.synchronize()
     assert K.read_status((M, 3072), 10, 256, 1024) == 0
-    ref = oracle_for(hidden, big_layer, tw, ids)
-    check_close(out, ref, None, f"M={M} path={path}")
+    ref = oracle_for(hidden, big_layer, tw, ids, path=path)
+    check_close(out, ref, None, f"M={M} path={path}",
+                PREFILL_OUTSIDE_FRAC_TOL if path == "prefill" else None)
     again = _run(K, big_layer, hidden, tw, ids)  # counters were left clean
     assert torch.equal(again, out)
 
@@ -225,7 +270,7 @@ def test_forward_prefill_token_subset(K, big_layer, M):
     torch.cuda.synchronize()
     toks = np.random.default_rng(M).choice(M, size=24, replace=False)
     ref = oracle_for(hidden, big_layer, tw, ids, tokens=toks)
-    check_close(out[torch.as_tensor(toks, device="cuda")], ref, None, f"M={M} (24 tokens)")
+    check_close(out[torch.as_tensor(toks, device="cuda")], ref, None, f"M={M} (24 tokens)", PREFILL_OUTSIDE_FRAC_TOL)
 
 
 def test_forward_prefill_m1024_all_rows(K, big_layer):
@@ -238,7 +283,7 @@ def test_forward_prefill_m1024_all_rows(K, big_layer):
     tw, ids = make_routing(M, 256, 10, device="cuda")
     out = _run(K, big_layer, hidden, tw, ids)
     torch.cuda.synchronize()
-    check_close(out, oracle_for(hidden, big_layer, tw, ids), None, "M=1024 all rows")
+    check_close(out, oracle_for(hidden, big_layer, tw, ids), None, "M=1024 all rows", PREFILL_OUTSIDE_FRAC_TOL)
 
 
 def test_apply_router_weight_on_input_and_inplace(K, big_layer):

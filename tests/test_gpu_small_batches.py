@@ -107,7 +107,9 @@ def test_small_expert_map(lib_, big_layer):  # noqa: F811
                    "w2_q": big_layer["w2_q"][sl], "w2_s": big_layer["w2_s"][sl]}
             check_close(out, oracle_for(hidden, sub, tw, ids, expert_map=emap), None, f"small shard {r}")
         total += out.float()
-    check_close(total.to(torch.bfloat16), oracle_for(hidden, big_layer, tw, ids), None, "small shards summed")
+    # three bf16-rounded shard outputs summed and rounded again: up to ~2 ulp
+    # from the one-pass reference, so the element count gets a stated bound
+    check_close(total.to(torch.bfloat16), oracle_for(hidden, big_layer, tw, ids), None, "small shards summed", 2e-2)
 
 
 def test_fused_agrees_with_general(K, big_layer):  # noqa: F811
@@ -124,4 +126,6 @@ def test_fused_agrees_with_general(K, big_layer):  # noqa: F811
     b = _run(K, big_layer, hidden, tw, ids)
     K.set_path("auto")
     torch.cuda.synchronize()
-    check_close(a, b.float().cpu().numpy(), None, "fused vs general")
+    # the two paths differ in weight numerics (exact (q - 8) vs bf16 (q - 8) * s),
+    # so only the norm-wise forms apply between them
+    check_close(a, b.float().cpu().numpy(), None, "fused vs general", outside_tol=1.0)
