@@ -70,9 +70,15 @@ constexpr int kPfErrWait = 16;  // error bit in sched[2]
 // trace layout [kind][1024] (CTA 0): 0 token rows of k issued, 1 dequant has
 // k's weights and a free A slot, 2 dequant published A(k), 3 MMA saw A and B
 // of k, 4 MMA committed k, 5 weights of k issued
+// Diagnostics builds only: otherwise the helper compiles to nothing (untaken
+// trace branches in the pipeline loops cost time).
+#ifdef W4A16_DIAGNOSTICS
 __device__ __forceinline__ void pf_trace(long long* tr, int kind, int k) {
   if (tr != nullptr && blockIdx.x == 0 && k < 1024) tr[kind * 1024 + k] = global_timer_ns();
 }
+#else
+__device__ __forceinline__ void pf_trace(long long*, int, int) {}
+#endif
 
 // Token-row tensor maps with box heights 32, 64, ..., 256 rows: each k-block's
 // rows arrive with a single tensor load (the per-load cost is ~45 SM clocks,
@@ -289,7 +295,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         wv[h] = lds128(stg + blk * 512 + fl * 16);
         sv[h] = lds64(stg + kPfScaleOff + blk * 64 + fg * 8);
       }
-      mbar_arrive(&w_empty[ws]);  // staging consumed (values are in registers)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const uint32_t sg0 = __byte_perm(sv[h].x, 0, 0x1010), sg80 = __byte_perm(sv[h].x, 0, 0x3232);
@@ -304,6 +309,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           for (int x = 0; x < 4; ++x) *reinterpret_cast<uint32_t*>(sth + aoff[j][x]) = a[x];
         }
       }
+      // The packed-weight staging is released only now, after the loaded words
+      // were consumed: arriving right after issuing the shared-memory loads let
+      // the next tensor load overwrite the staging under them (a fraction of
+      // 16-row A blocks came out nondeterministic at large M).
+      mbar_arrive(&w_empty[ws]);
       fence_proxy_async_shared();  // generic smem writes -> tensor-core reads
       mbar_arrive(&a_full[s]);
       if (gt == 0) pf_trace(p.trace, 2, k);
