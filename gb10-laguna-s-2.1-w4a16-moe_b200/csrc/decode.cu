@@ -67,11 +67,17 @@ enum DecodeError : int {
   kErrRedWait = 8,
 };
 
-struct StageInfo {
+// Per-stage descriptor written by the producer: everything the consumer warps
+// need, so that they do no integer division per stage.
+struct __align__(16) StageInfo {
   int item;  // -1 = end of work
   int pass;
   int part;
-  int pad;
+  int last;  // last part of the item pass
+  int nc;    // k-chunks in the stage
+  int R;     // row tiles of the item
+  int lgw;   // log2(consumer warps per tile group)
+  int rows;  // activation rows (slots) of the pass
 };
 
 struct Geometry {
@@ -83,12 +89,24 @@ struct Geometry {
 // Row tiles per consumer warp: keeps Rw * NG * 4 accumulators <= 16.
 __host__ __device__ constexpr int rows_per_warp(int NG) { return NG == 4 ? 1 : 2; }
 
-// trace layout: [kind][512]; kinds 0 = producer stage issued, 1 = consumer
-// warp 0 stage data landed, 2 = consumer warp 0 stage done, 3 = epilogue 0
-// start, 4 = epilogue 0 end, 5 = kernel start / prologue end / teardown
+// Pipeline timestamps (diagnostics builds only: without W4A16_DIAGNOSTICS the
+// helpers compile to nothing, since even untaken trace branches in the hot
+// loops measurably slowed the kernel).  Layout: [kind][512] for CTA 0 (0
+// producer stage issued, 1 consumer warp 0 stage landed, 2 consumer warp 0
+// stage done, 3/4 epilogue 0 start/end, 5 kernel start / prologue end /
+// teardown), then per-CTA milestones [cta][32] (0 start, 1 prologue end, 4
+// producer done, 6 consumer warp 0 done, 9 end).
+#ifdef W4A16_DIAGNOSTICS
 __device__ __forceinline__ void trace_ev(long long* tr, int kind, int k) {
   if (tr != nullptr && blockIdx.x == 0 && k < 512) tr[kind * 512 + k] = global_timer_ns();
 }
+__device__ __forceinline__ void trace_cta(long long* tr, int k) {
+  if (tr != nullptr) tr[6 * 512 + blockIdx.x * 32 + k] = global_timer_ns();
+}
+#else
+__device__ __forceinline__ void trace_ev(long long*, int, int) {}
+__device__ __forceinline__ void trace_cta(long long*, int) {}
+#endif
 
 __device__ __forceinline__ void record_error(int* sched, int code) { atomicOr(sched + kSchedError, code); }
 
@@ -102,6 +120,17 @@ struct ItemView {
   int T;     // slots routed to e
   int base;  // start of e's slots in the per-CTA slot list
 };
+
+// Shared-memory offset of this lane's ldmatrix row address within a stage's
+// activation rows (row stride bstride = 16 mod 128, so the eight rows of one
+// 8x8 matrix fall in distinct 16-byte bank groups).  Lanes whose row is not
+// reserved (row >= nrows) read row 0 at a rotated 16-byte column: those
+// columns of the product are never used, and distinct addresses keep the
+// load conflict-free.
+__device__ __forceinline__ int brow_off(int lane, int nrows, int bstride) {
+  const int r = lane & 7, j = lane >> 3;
+  return r < nrows ? r * bstride + j * 16 : ((j + r) & 7) * 16;
+}
 
 __host__ __device__ __forceinline__ int stage_bytes_for(int R, int nc, int rows) {
   return R * nc * 576 + rows * (nc * 128 + 16);
@@ -125,6 +154,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
   __shared__ StageInfo sinfo[kDecMaxStages];
   __shared__ StageInfo rinfo[kDecEpiWarps];
   __shared__ int s_nact;
+  __shared__ int s_wtot[32], s_wact[32], s_wmax[32];
+  __shared__ int s_last;
   __shared__ Geometry s_geo;
   extern __shared__ __align__(128) unsigned char dsm[];
 
@@ -144,16 +175,20 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
   const int n_red = p.n_red;
 
   // ---------------- prologue: barriers + routing tables ----------------
+  // The first top-k id of each thread is loaded before anything else, so its
+  // global-memory latency overlaps the barrier set-up.
+  const int my_e = tid < p.n_tok ? p.map(tid) : -1;
   if (tid == 0) {
     trace_ev(p.trace, 5, 0);
-    for (int s = 0; s < kDecMaxStages; ++s) {
-      mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], kDecConsumers);
-    }
-    for (int b = 0; b < kDecEpiWarps; ++b) {
-      mbar_init(&red_full[b], kDecConsumers);
-      mbar_init(&red_empty[b], 1);
-    }
+    trace_cta(p.trace, 0);
+  }
+  if (tid < kDecMaxStages) {
+    mbar_init(&full_bar[tid], 1);
+    mbar_init(&empty_bar[tid], kDecConsumers);
+    fence_barrier_init();
+  } else if (tid >= 32 && tid < 32 + kDecEpiWarps) {
+    mbar_init(&red_full[tid - 32], kDecConsumers);
+    mbar_init(&red_empty[tid - 32], 1);
     fence_barrier_init();
   }
   for (int e = tid; e < E; e += kDecThreads) cnt[e] = 0;
@@ -161,7 +196,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
   for (int w = tid; w <= p.n_tok / 32; w += kDecThreads) sok[w] = 0;
   __syncthreads();
   for (int i = tid; i < p.n_tok; i += kDecThreads) {
-    const int e = p.map(i);
+    const int e = i == tid ? my_e : p.map(i);
     eid[i] = e;
     if (e >= 0) {
       atomicAdd(&cnt[e], 1);
@@ -170,46 +205,65 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
     }
   }
   __syncthreads();
-  if (warp == 0) {  // exclusive scans of counts and of (count > 0); max count
-    int run = 0, nact = 0, mx = 0;
-    for (int e0 = 0; e0 < E; e0 += 32) {
-      const int e = e0 + lane;
-      const int c = e < E ? cnt[e] : 0;
-      mx = max(mx, c);
-      int inc = c, ia = c > 0;
+  // Exclusive scans of the counts and of (count > 0), and the largest count,
+  // by all warps: warp w scans experts [32w, 32w + 32) (pass 1), then adds the
+  // totals of the warps before it (pass 2).
+  constexpr int kWarps = kDecThreads / 32;
+  const int nEw = (E + 31) / 32;  // <= 32 (E <= 1024)
+  const unsigned lanes_le = 0xffffffffu >> (31 - lane);
+  for (int w = warp; w < nEw; w += kWarps) {
+    const int e = w * 32 + lane;
+    const int c = e < E ? cnt[e] : 0;
+    int inc = c;
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int a = __shfl_up_sync(0xffffffffu, inc, o);
-        const int b = __shfl_up_sync(0xffffffffu, ia, o);
-        if (lane >= o) {
-          inc += a;
-          ia += b;
-        }
-      }
-      if (e < E) {
-        off[e] = run + inc - c;
-        cur[e] = run + inc - c;
-        if (c > 0) act[nact + ia - 1] = e;
-      }
-      run += __shfl_sync(0xffffffffu, inc, 31);
-      nact += __shfl_sync(0xffffffffu, ia, 31);
+    for (int o = 1; o < 32; o <<= 1) {
+      const int a = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += a;
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0) {
-      off[E] = run;
-      s_nact = nact;
-      // stage geometry: the largest stages that still fit three in the ring
-      // stage geometry for this many reserved activation rows, precomputed
-      // on the host (decode_plan) for every row count 1..NB
-      const int rr = max(1, min(NB, mx));
-      Geometry gm;
-      gm.rows_res = rr;
-      gm.ncA = p.geo[rr][0];
-      gm.ncB = p.geo[rr][1];
-      gm.stage_bytes = p.geo[rr][2];
-      gm.n_stages = p.geo[rr][3];
-      s_geo = gm;
+    const unsigned actm = __ballot_sync(0xffffffffu, c > 0);
+    if (e < E) {
+      off[e] = inc - c;                                   // local exclusive offset
+      cur[e] = c > 0 ? __popc(actm & lanes_le) - 1 : -1;  // local active rank
+    }
+    const int mx = (int)__reduce_max_sync(0xffffffffu, (unsigned)c);
+    if (lane == 31) {
+      s_wtot[w] = inc;
+      s_wact[w] = __popc(actm);
+      s_wmax[w] = mx;
+    }
+  }
+  __syncthreads();
+  for (int w = warp; w < nEw; w += kWarps) {
+    const int e = w * 32 + lane;
+    const int tot = lane < w ? s_wtot[lane] : 0, na = lane < w ? s_wact[lane] : 0;
+    const int base = (int)__reduce_add_sync(0xffffffffu, (unsigned)tot);
+    const int abase = (int)__reduce_add_sync(0xffffffffu, (unsigned)na);
+    if (e < E) {
+      const int o = off[e] + base;
+      off[e] = o;
+      if (cur[e] >= 0) act[abase + cur[e]] = e;
+      cur[e] = o;
+    }
+    if (w == 0) {
+      const int t = lane < nEw ? s_wtot[lane] : 0, a = lane < nEw ? s_wact[lane] : 0;
+      const int m = lane < nEw ? s_wmax[lane] : 0;
+      const int run = (int)__reduce_add_sync(0xffffffffu, (unsigned)t);
+      const int nact = (int)__reduce_add_sync(0xffffffffu, (unsigned)a);
+      const int mxall = (int)__reduce_max_sync(0xffffffffu, (unsigned)m);
+      if (lane == 0) {
+        off[E] = run;
+        s_nact = nact;
+        // stage geometry for this many reserved activation rows, precomputed
+        // on the host (decode_plan) for every row count 1..NB
+        const int rr = max(1, min(NB, mxall));
+        Geometry gm;
+        gm.rows_res = rr;
+        gm.ncA = p.geo[rr][0];
+        gm.ncB = p.geo[rr][1];
+        gm.stage_bytes = p.geo[rr][2];
+        gm.n_stages = p.geo[rr][3];
+        s_geo = gm;
+      }
     }
   }
   __syncthreads();
@@ -222,7 +276,10 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
           *reinterpret_cast<uint4*>(p.out + (size_t)m * p.H + h) = make_uint4(0, 0, 0, 0);
   }
   __syncthreads();
-  if (tid == 0) trace_ev(p.trace, 5, 1);
+  if (tid == 0) {
+    trace_ev(p.trace, 5, 1);
+    trace_cta(p.trace, 1);
+  }
 
   const Geometry geo = s_geo;
   const int nact = s_nact;
@@ -278,7 +335,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
           }
           unsigned char* buf = ring + (size_t)stage * geo.stage_bytes;
           if (lane == 0) {
-            sinfo[stage] = StageInfo{done ? -1 : item, pass, part, 0};
+            sinfo[stage] = StageInfo{done ? -1 : item, pass, part, part == parts - 1, nc, R,
+                                     31 - __clz(kDecConsumers / (R / RW)), rows};
             const uint32_t tx = done ? 0u : (uint32_t)R * (wbytes + sbytes) + (uint32_t)rows * bbytes;
             if (tx) mbar_arrive_expect_tx(&full_bar[stage], tx);
             else mbar_arrive(&full_bar[stage]);
@@ -333,14 +391,13 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
       }
       if (done) break;
     }
+    if (lane == 0) trace_cta(p.trace, 4);
   } else if (warp < kDecConsumers) {
     // ======================= consumer warps =======================
     const int g = lane >> 2, t = lane & 3;
     int stage = 0, rb = 0;
     uint32_t uses = 0, ruses = 0;  // stages consumed; item passes handed off
     float acc[RW][NG][4];
-    int cur_item = -1;
-    ItemView v{};
     while (true) {
       if (!mbar_wait(&full_bar[stage], (uses / S) & 1, kWaitBudget)) {
         if (lane == 0) record_error(p.sched, kErrFullWait);
@@ -356,24 +413,18 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
             if (lane == 0) record_error(p.sched, kErrRedWait);
             break;
           }
-          if (warp == 0 && lane == 0) rinfo[rb] = StageInfo{-1, 0, 0, 0};
+          if (warp == 0 && lane == 0) rinfo[rb] = StageInfo{-1, 0, 0, 0, 0, 0, 0, 0};
           __syncwarp();
           if (lane == 0) mbar_arrive(&red_full[rb]);
           ++ruses;
           rb = (rb + 1 == n_red) ? 0 : rb + 1;
         }
+        if (warp == 0 && lane == 0) trace_cta(p.trace, 6);
         break;
       }
-      if (si.item != cur_item) {
-        v = view(si.item);
-        cur_item = si.item;
-      }
-      const int parts = v.phB ? partsB : partsA;
-      const int nc = v.phB ? geo.ncB : geo.ncA;
-      const int R = v.phB ? p.R2 : 2 * p.RP;
-      const int ngrp = R / RW;                 // tile groups per item
-      const int wpg = kDecConsumers / ngrp;    // warps per tile group
-      const int tg = warp / wpg, cw = warp - tg * wpg;
+      const int nc = si.nc, R = si.R;
+      const int wpg = 1 << si.lgw;  // warps per tile group
+      const int tg = warp >> si.lgw, cw = warp & (wpg - 1);
       if (si.part == 0) {
 #pragma unroll
         for (int i = 0; i < RW; ++i)
@@ -387,12 +438,10 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
       const unsigned char* sc = buf + (size_t)R * nc * 512 + (size_t)(tg * RW) * nc * 64 + g * 8;
       const unsigned char* bs = buf + (size_t)R * nc * 576;
       const int bstride = nc * 128 + 16;
-      const int rows = min(NB, v.T - si.pass * NB);
-      const int lrow = lane & 7;
+      const int rows = si.rows;
       for (int c = cw; c < nc; c += wpg) {
         if constexpr (NG == 1) {
-          const unsigned char* brow =
-              bs + (size_t)(lrow < geo.rows_res ? lrow : 0) * bstride + c * 128 + (lane >> 3) * 16;
+          const unsigned char* brow = bs + brow_off(lane, geo.rows_res, bstride) + c * 128;
           uint32_t b0[4], b1[4];
           ldmatrix_x4(b0, brow);
           ldmatrix_x4(b1, brow + 64);
@@ -433,9 +482,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
 #pragma unroll
           for (int qq = 0; qq < NG; ++qq) {
             if (qq * 8 >= rows) break;
-            const int rr = qq * 8 + lrow;
-            const unsigned char* brow =
-                bs + (size_t)(rr < geo.rows_res ? rr : 0) * bstride + c * 128 + (lane >> 3) * 16;
+            const unsigned char* brow = bs + brow_off(lane, geo.rows_res - qq * 8, bstride) + qq * 8 * bstride + c * 128;
             uint32_t b0[4], b1[4];
             ldmatrix_x4(b0, brow);
             ldmatrix_x4(b1, brow + 64);
@@ -454,7 +501,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
       if (warp == 0 && lane == 0) trace_ev(p.trace, 2, (int)uses);
       ++uses;
       stage = (stage + 1 == S) ? 0 : stage + 1;
-      if (si.part != parts - 1) continue;
+      if (!si.last) continue;
 
       // end of an item pass: hand the accumulators to an epilogue warp
       const uint32_t ru = ruses / n_red;
@@ -645,13 +692,18 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
   __syncthreads();
   if (tid == 0) {
     trace_ev(p.trace, 5, 2);
+    trace_cta(p.trace, 9);
     __threadfence();
-    if (atomicAdd(p.sched + kSchedDone, 1) == (int)gridDim.x - 1) {
+    s_last = atomicAdd(p.sched + kSchedDone, 1) == (int)gridDim.x - 1;
+  }
+  __syncthreads();
+  if (s_last) {
+    for (int e = tid; e < E; e += kDecThreads) p.ready[e] = 0;
+    if (tid == 0) {
       p.sched[kSchedDone] = 0;
       p.sched[kSchedBDone] = 0;
-      for (int e = 0; e < E; ++e) p.ready[e] = 0;
-      __threadfence();
     }
+    __threadfence();
   }
 }
 
