@@ -134,7 +134,11 @@ def _dist():
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        import datetime
+
+        # a collective that one rank never joins fails in two minutes, not ten
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=datetime.timedelta(seconds=120))
     return world, rank, local
 
 
@@ -631,12 +635,13 @@ def run_ep(args) -> int:
 
     # ---- parity spot check (rank 0, untimed): layer 0 on 4 of its tokens vs the oracle ----
     parity = None
+    # the layer's exchange is a collective: every rank runs it, rank 0 checks
+    x1 = None if args.no_parity else ep.moe_layer(x0, routing[0][0], routing[0][1], layers[0], E, emap, capacity=cap)
     if rank == 0 and not args.no_parity:
         import numpy as np
 
         from oracle import moe_oracle as O
 
-        x1 = ep.moe_layer(x0, routing[0][0], routing[0][1], layers[0], E, emap, capacity=cap)
         sub_tok = 4
         ids_s = routing[0][1][:sub_tok].to(torch.int64).cpu()
         tw_s = routing[0][0][:sub_tok].float().cpu().numpy()
