@@ -169,7 +169,7 @@ int w4a16_moe_read_status(const void* workspace, int64_t M, int64_t topk, int64_
 
 int w4a16_set_wait_test(int mode) {
   g_last_error.clear();
-  if (mode < 0 || mode > 1) return fail(kInvalidArgument, "w4a16_set_wait_test: mode 0 or 1");
+  if (mode < 0 || mode > 2) return fail(kInvalidArgument, "w4a16_set_wait_test: mode 0, 1 or 2");
   g_wait_test = mode;
   return kOk;
 }
@@ -369,6 +369,10 @@ int w4a16_moe_forward(const void* hidden, int64_t M, int64_t H, int64_t hidden_l
     if (const char* tr = getenv("W4A16_DECODE_TRACE")) dp.trace = (long long*)strtoull(tr, nullptr, 0);
 #endif
     if (decode_plan(dp, sm_count(), max_smem_optin() - 1024)) {
+      if (g_wait_test == 2) {  // test hook: readiness withheld, ~10 us waits
+        dp.withhold = 1;
+        dp.ready_budget = 20000;
+      }
       mark_stage(0, st);
       mark_stage(1, st);
       cudaError_t err = launch_decode(dp, st);

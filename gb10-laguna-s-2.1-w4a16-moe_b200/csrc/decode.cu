@@ -363,7 +363,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
                 const int target = PA * passes;
                 const long long t0 = clock64();
                 while (ld_acquire_gpu(p.ready + v.e) < target) {
-                  if (clock64() - t0 > kWaitBudget) {
+                  if (clock64() - t0 > p.ready_budget) {
                     record_error(p.sched, kErrReadyWait);
                     break;
                   }
@@ -577,7 +577,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
         if (lane == 0) mbar_arrive(&red_empty[rb]);  // buffer no longer read
         __threadfence();
         __syncwarp();
-        if (lane == 0) atomicAdd(p.ready + v.e, 1);
+        if (lane == 0 && !(p.withhold && blockIdx.x == 0)) atomicAdd(p.ready + v.e, 1);
       } else {
         const int R2 = p.R2, span = R2 * 16;
         for (int idx = lane; idx < R2 * NG * 32; idx += 32) {
@@ -734,6 +734,8 @@ int decode_plan(DecodeParams& p, int sms, int max_smem) {
   // grid-wide top-k sum after all w2 items (measured faster than the
   // per-(token, row block) last-arriver sum at every M on B200)
   p.tail_reduce = 1;
+  p.ready_budget = kWaitBudget;
+  p.withhold = 0;
 #ifdef W4A16_DIAGNOSTICS
   if (const char* e = getenv("W4A16_DECODE_TAIL")) p.tail_reduce = atoi(e);
 #endif

@@ -98,6 +98,8 @@ struct DecodeParams {
   int32_t* sched;            // [4] next item, finished CTAs, error bits
   int zero_rows;             // write zero rows for tokens with no local slot
   int tail_reduce;           // 1: grid-wide top-k sum after all w2 items; 0: per-token last arriver
+  long long ready_budget;    // SM clocks a w2 item waits for its expert's intermediate (set by decode_plan)
+  int withhold;              // test hook: CTA 0 publishes no w13 readiness (the waits then run out)
   long long* trace;          // optional event timestamps of CTA 0 (diagnostics; nullptr normally)
   // plan (decode_plan); the stage geometry is derived per CTA on the device
   int NG, RP, R2, n_red, red_offset, ring_offset, ring_bytes, smem_bytes, grid;

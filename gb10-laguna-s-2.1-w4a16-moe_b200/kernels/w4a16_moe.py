@@ -351,8 +351,16 @@ def moe_align_block_size(
 _WS_CACHE: dict[tuple, torch.Tensor] = {}
 
 
+def _device_key(device: torch.device | str) -> str:
+    """Cache key of a device: "cuda" and "cuda:<current>" name the same one."""
+    d = torch.device(device)
+    if d.type == "cuda" and d.index is None:
+        d = torch.device("cuda", torch.cuda.current_device())
+    return str(d)
+
+
 def _workspace(device: torch.device, M: int, topk: int, E: int, H: int, I: int) -> torch.Tensor:
-    key = (str(device), M, topk, E, H, I)
+    key = (_device_key(device), M, topk, E, H, I)
     ws = _WS_CACHE.get(key)
     if ws is None:
         nbytes = int(load_library().w4a16_moe_workspace_size(M, topk, E, H, I))
@@ -395,7 +403,7 @@ def read_status(hidden_shape: tuple[int, int], topk: int, num_experts: int, inte
     """Read and clear the error bits recorded in the pooled workspace of a
     forward shape (0 = no bounded wait timed out).  Synchronises."""
     M, H = hidden_shape
-    ws = _WS_CACHE.get((str(torch.device(device)), M, topk, num_experts, H, intermediate))
+    ws = _WS_CACHE.get((_device_key(device), M, topk, num_experts, H, intermediate))
     if ws is None:
         return 0
     out = ctypes.c_int32(0)

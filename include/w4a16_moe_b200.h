@@ -111,7 +111,10 @@ W4A16_API int w4a16_moe_align_read_status(void* scratch, int32_t* status_out, vo
  * Test hook for the bounded device waits (no reference counterpart): mode 1
  * makes the calling thread's next multi-CTA align launches withhold one CTA's
  * arrival at the grid barrier and wait only ~10 us, so the wait runs out and
- * the timeout is reported as status; mode 0 restores normal operation.
+ * the timeout is reported as status; mode 2 makes the fused decode kernel's
+ * CTA 0 publish none of its w13 items and the w2 items wait only ~10 us for
+ * them, so those waits run out, the call finishes with wrong values and
+ * w4a16_moe_read_status reports bit 4; mode 0 restores normal operation.
  */
 W4A16_API int w4a16_set_wait_test(int mode);
 

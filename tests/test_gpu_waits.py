@@ -3,7 +3,10 @@ leaves the GPU usable.  The multi-CTA align kernel's grid barrier is made to
 time out on purpose through the library's test hook (one CTA withholds its
 arrival, the others wait ~10 us), with no fault, trap or unbounded wait; the
 timeout must appear in w4a16_moe_align_read_status, and the same scratch must
-give bit-exact results on the next normal call."""
+give bit-exact results on the next normal call.  The fused decode kernel's
+per-expert readiness wait is made to run out the same way (CTA 0 publishes
+none of its w13 items, the w2 items wait ~10 us): the call returns, the error
+bit is reported, and the next normal call is bit-exact."""
 
 from __future__ import annotations
 
@@ -82,3 +85,36 @@ def test_align_barrier_timeout_is_reported(lib):
     np.testing.assert_array_equal(s.cpu().numpy(), rs)
     np.testing.assert_array_equal(e.cpu().numpy(), re_)
     np.testing.assert_array_equal(n.cpu().numpy(), rn)
+
+
+DECODE_READY_WAIT_BIT = 4
+
+
+def test_decode_readiness_timeout_is_reported(lib):
+    from kernels import w4a16_moe as K
+    from kernels.synthetic import make_hidden, make_layer, make_routing
+
+    E, H, I, M = 256, 3072, 1024, 1
+    layer = make_layer(E, H, I, seed=0, device="cuda")
+    w1r, s1r = K.repack_weights(layer["w1_q"], layer["w1_s"])
+    w2r, s2r = K.repack_weights(layer["w2_q"], layer["w2_s"])
+    del layer
+    hidden = make_hidden(M, H, device="cuda")
+    tw, ids = make_routing(M, E, 10, device="cuda")
+    ref = K.fused_experts_w4a16(hidden, w1r, w2r, s1r, s2r, tw, ids).clone()
+    torch.cuda.synchronize()
+    assert K.read_status((M, H), 10, E, I) == 0
+
+    assert lib.w4a16_set_wait_test(2) == 0
+    try:
+        K.fused_experts_w4a16(hidden, w1r, w2r, s1r, s2r, tw, ids)
+        torch.cuda.synchronize()
+    finally:
+        assert lib.w4a16_set_wait_test(0) == 0
+    assert K.read_status((M, H), 10, E, I) & DECODE_READY_WAIT_BIT
+
+    # counters were reset by the timed-out call: the next one is exact again
+    again = K.fused_experts_w4a16(hidden, w1r, w2r, s1r, s2r, tw, ids)
+    torch.cuda.synchronize()
+    assert K.read_status((M, H), 10, E, I) == 0
+    assert torch.equal(again, ref)
