@@ -51,9 +51,10 @@
 namespace w4moe {
 
 constexpr int kDecConsumers = 16;
-constexpr int kDecProducerWarp = kDecConsumers;
+constexpr int kDecProducerWarp = kDecConsumers;  // first of kDecProducers producer warps
+constexpr int kDecProducers = 2;                  // producer p issues the stages g with g % 2 == p
 constexpr int kDecEpiWarps = 4;  // epilogue warp k owns reduction buffer k (k < n_red)
-constexpr int kDecThreads = (kDecConsumers + 1 + kDecEpiWarps) * 32;
+constexpr int kDecThreads = (kDecConsumers + kDecProducers + kDecEpiWarps) * 32;
 constexpr int kDecMaxStages = 8;
 constexpr long long kWaitBudget = 4000000000LL;  // ~2 s of SM clocks
 
@@ -304,8 +305,12 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
     return v;
   };
 
-  if (warp == kDecProducerWarp) {
-    // ======================= producer warp =======================
+  if (warp >= kDecProducerWarp && warp < kDecProducerWarp + kDecProducers) {
+    // ======================= producer warps =======================
+    // Both walk the same stage sequence; producer pid issues the stages
+    // g with g % kDecProducers == pid, so one stage's copy issue, readiness
+    // check and item switch overlap the other's.
+    const int pid = warp - kDecProducerWarp;
     const uint64_t pol = l2_evict_first_policy();
     int stage = 0;
     uint32_t uses = 0;  // stages issued so far (barrier parities)
@@ -328,6 +333,12 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
       for (int pass = 0; pass < passes && !abort; ++pass) {
         const int rows = done ? 0 : min(NB, v.T - pass * NB);
         for (int part = 0; part < parts; ++part) {
+          if ((int)(uses % kDecProducers) != pid) {  // the other producer's stage
+            ++uses;
+            stage = (stage + 1 == S) ? 0 : stage + 1;
+            if (done) break;
+            continue;
+          }
           if (uses >= (uint32_t)S && !mbar_wait(&empty_bar[stage], ((uses / S) - 1) & 1, kWaitBudget)) {
             if (lane == 0) record_error(p.sched, kErrEmptyWait);
             abort = true;
@@ -526,9 +537,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
       ++ruses;
       rb = (rb + 1 == n_red) ? 0 : rb + 1;
     }
-  } else if (warp - kDecConsumers - 1 < n_red) {
+  } else if (warp - kDecConsumers - kDecProducers < n_red) {
     // ======================= epilogue warps =======================
-    const int rb = warp - kDecConsumers - 1;  // this warp's reduction buffer
+    const int rb = warp - kDecConsumers - kDecProducers;  // this warp's reduction buffer
     const float* rbuf = red + (size_t)rb * kRedFloats;
     uint32_t ru = 0;
     while (true) {
