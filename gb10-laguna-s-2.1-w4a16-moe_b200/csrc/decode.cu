@@ -52,7 +52,7 @@ namespace w4moe {
 
 constexpr int kDecConsumers = 16;
 constexpr int kDecProducerWarp = kDecConsumers;  // first of kDecProducers producer warps
-constexpr int kDecProducers = 2;                  // producer p issues the stages g with g % 2 == p
+constexpr int kDecProducers = 2;                  // producer p refills the ring slots s with s % 2 == p
 constexpr int kDecEpiWarps = 4;  // epilogue warp k owns reduction buffer k (k < n_red)
 constexpr int kDecThreads = (kDecConsumers + kDecProducers + kDecEpiWarps) * 32;
 constexpr int kDecMaxStages = 8;
@@ -307,9 +307,13 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
 
   if (warp >= kDecProducerWarp && warp < kDecProducerWarp + kDecProducers) {
     // ======================= producer warps =======================
-    // Both walk the same stage sequence; producer pid issues the stages
-    // g with g % kDecProducers == pid, so one stage's copy issue, readiness
-    // check and item switch overlap the other's.
+    // Both walk the same stage sequence; producer pid issues the stages whose
+    // ring slot s has s % kDecProducers == pid, so one stage's copy issue,
+    // readiness check and item switch overlap the other's.  Ownership is by
+    // slot, not by stage: a slot is always refilled by the same producer, in
+    // order, so its parity wait for the previous use of the slot can never
+    // see a phase two uses old (stages dealt round robin to more producers
+    // than slots aliased that wait and corrupted the barriers).
     const int pid = warp - kDecProducerWarp;
     const uint64_t pol = l2_evict_first_policy();
     int stage = 0;
@@ -333,7 +337,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) moe_decode_fused_kernel(Decode
       for (int pass = 0; pass < passes && !abort; ++pass) {
         const int rows = done ? 0 : min(NB, v.T - pass * NB);
         for (int part = 0; part < parts; ++part) {
-          if ((int)(uses % kDecProducers) != pid) {  // the other producer's stage
+          if (stage % kDecProducers != pid) {  // another producer's slot
             ++uses;
             stage = (stage + 1 == S) ? 0 : stage + 1;
             if (done) break;
