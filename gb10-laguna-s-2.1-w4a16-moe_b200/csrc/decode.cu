@@ -732,8 +732,10 @@ int decode_plan(DecodeParams& p, int sms, int max_smem) {
   // item sizes (row tiles per w13 / w2 item), measured on B200 at E=256
   // top-10 3072x1024: larger items amortise per-item handoffs until too few
   // items remain to balance over the SMs
-  int RP = M <= 16 ? 2 : 4;
-  int R2 = M <= 16 ? 4 : 8;
+  // (with two producer warps: one gate/up pair per w13 item up to M=8, w2
+  // items of 4 row tiles at M=1 and 9..16, 8 otherwise)
+  int RP = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
+  int R2 = (M == 1 || (M > 8 && M <= 16)) ? 4 : 8;
 #ifdef W4A16_DIAGNOSTICS
   if (const char* e = getenv("W4A16_DECODE_RP")) RP = atoi(e);
   if (const char* e = getenv("W4A16_DECODE_R2")) R2 = atoi(e);
