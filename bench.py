@@ -548,6 +548,12 @@ def run_ep(args) -> int:
     own = ep.owned_experts(E, world, rank)
     emap = ep.local_expert_map(E, world, rank, dev)
     bias = zipf_bias(E, 1.1, seed=0)
+    perm = None
+    if args.placement == "balanced" and world > 1:
+        # load-aware placement from a calibration batch of the same routing
+        # distribution (another seed): a load-time relabelling of the experts
+        _, calib = make_routing(EP_TOKENS, E, TOPK, seed=424_242, device="cpu", bias=bias)
+        perm = ep.balanced_placement(torch.bincount(calib.flatten().long(), minlength=E), world).to(dev)
     layers, routing = [], []
     for l in range(EP_LAYERS):
         lay = make_layer(len(own), H, I, seed=1000 * l + rank, device=dev)  # this rank's experts only
@@ -556,6 +562,8 @@ def run_ep(args) -> int:
         del lay
         layers.append(ep.LocalExperts(w1r, s1r, w2r, s2r))
         tw, ids = make_routing(m_src, E, TOPK, seed=7919 * l + 31 * rank, device=dev, bias=bias)
+        if perm is not None:  # what the permuted router emits
+            ids = perm[ids.long()].to(torch.int32)
         routing.append((tw, ids))
     x0 = make_hidden(m_src, H, seed=rank, device=dev)
     # fixed-capacity exchange (no host read of counts) unless asked otherwise
@@ -694,6 +702,7 @@ def run_ep(args) -> int:
             "config": {"workload": EP_WORKLOAD,
                        "tokens_per_step": EP_TOKENS, "layers": EP_LAYERS, "experts_per_rank": len(own),
                        "parallelism": f"ep{world}", "exchange": args.ep_exchange,
+                       "placement": args.placement if world > 1 else "single rank",
                        "l2": "inputs larger than L2 (each layer's expert weights stream from HBM)",
                        "timing": "CUDA events around all steps on each rank, max over ranks",
                        "nvlink_bytes_per_step_max_rank": max_sent,
@@ -733,6 +742,9 @@ def main(argv=None) -> int:
                          "(default: ep when launched by torchrun, decode otherwise)")
     ap.add_argument("--no-parity", action="store_true", help="skip the untimed parity spot check")
     ap.add_argument("--no-sweep", action="store_true", help="skip the configuration 2/3 sweep of the N=1 line")
+    ap.add_argument("--placement", choices=["balanced", "contiguous"], default="balanced",
+                    help="expert-parallel expert placement: balanced by calibration load (a load-time "
+                         "relabelling) or contiguous id ranges")
     ap.add_argument("--ep-exchange", choices=["fixed", "counts"], default="fixed",
                     help="ep: fixed-capacity all-to-all (no host sync) or exact counts read back to the host")
     args = ap.parse_args(argv)

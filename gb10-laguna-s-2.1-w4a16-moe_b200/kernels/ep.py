@@ -60,6 +60,37 @@ def owned_experts(num_experts: int, world: int, rank: int) -> range:
     return range(rank * per, (rank + 1) * per)
 
 
+def balanced_placement(load: torch.Tensor, world: int) -> torch.Tensor:
+    """Expert placement balanced by measured load, as a relabelling.
+
+    ``load[e]`` is how many routed slots expert ``e`` received on a
+    calibration batch.  Returns ``perm`` (int64 [E]) with ``perm[e]`` the
+    placed id of expert ``e``; rank r then owns the placed ids
+    [r * E / G, (r + 1) * E / G) exactly as in :func:`owned_experts`, so the
+    exchange kernels are unchanged.  A deployment applies it once at load
+    time: permute the router's output rows (the router then emits placed ids)
+    and store expert ``e``'s weights at position ``perm[e]``.
+
+    Greedy and deterministic: experts in descending load (ties: lower id) go
+    to the rank with the smallest total so far among ranks with a free slot
+    (ties: lower rank); each rank takes exactly E / G experts.
+    """
+    E = load.numel()
+    assert E % world == 0, "experts must divide evenly over ranks"
+    per = E // world
+    ld = load.detach().to("cpu", torch.float64)
+    order = sorted(range(E), key=lambda e: (-float(ld[e]), e))
+    total = [0.0] * world
+    fill = [0] * world
+    perm = torch.empty(E, dtype=torch.int64)
+    for e in order:
+        r = min((x for x in range(world) if fill[x] < per), key=lambda x: (total[x], x))
+        perm[e] = r * per + fill[r]
+        fill[r] += 1
+        total[r] += float(ld[e])
+    return perm
+
+
 def local_expert_map(num_experts: int, world: int, rank: int, device) -> torch.Tensor:
     """vLLM-style ``expert_map``: global id -> local id, or -1 if not owned."""
     emap = torch.full((num_experts,), -1, dtype=torch.int32)
