@@ -81,10 +81,6 @@ __device__ __forceinline__ void dequant_word(uint32_t w, uint32_t sg, uint32_t s
   a[3] = bf16x2_mul(bf16x2_sub(and_or(w >> 12, kMask, kMagic), kBias), sg8);
 }
 
-__device__ __forceinline__ uint32_t bcast_bf16(uint16_t s) {
-  return (uint32_t)s | ((uint32_t)s << 16);
-}
-
 // D = A(16x16 bf16, row) * B(16x8 bf16, col) + D, fp32 accumulate.
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4],
                                                uint32_t b0, uint32_t b1) {
@@ -191,18 +187,6 @@ __device__ __forceinline__ void fence_proxy_async_shared() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// ---- cp.async (16-byte, L2 only) with zero fill ----
-__device__ __forceinline__ void cp_async16_zfill(void* dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
-               "r"(valid ? 16 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait_group() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
 // ---- tcgen05 (5th-gen tensor core, accumulators in TMEM) ----
 
 // Byte offset of bf16 element (r, k) inside a [rows x 64] K-major operand
@@ -301,21 +285,6 @@ __device__ __forceinline__ void tma_load_2d_u32(uint32_t dst, const void* tmap, 
       : "memory");
 }
 
-// L2 prefetch of a 2-D tensor box (no shared memory, no completion).
-__device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int x, int y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(tmap), "r"(x), "r"(y)
-               : "memory");
-}
-
-// 3-D tiled tensor load (TMA) of box at {x, y, z} completing on `bar`.
-__device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int x, int y, int z, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
-          smem_u32(dst)),
-      "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
-      : "memory");
-}
-
 __device__ __forceinline__ void tma_load_3d_u32(uint32_t dst, const void* tmap, int x, int y, int z, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
@@ -342,12 +311,6 @@ __device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32
           smem_u32(dst)),
       "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
-}
-
-// L2 prefetch of a contiguous global range (16-byte aligned, size % 16 == 0);
-// no shared memory, no completion to wait for.
-__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ void fence_proxy_async_global() {
