@@ -15,14 +15,16 @@
 //     all phase-A items precede all phase-B items.  An item's K range is cut
 //     into parts that fit one pipeline stage; an expert with more slots than
 //     one pass holds (8*NG) is done in passes.
-//   * producer warp: per stage, cp.async.bulk of the item's weight and scale
+//   * 2 producer warps, each owning one ring slot (both walk the same stage
+//     sequence; one stage's issue overlaps the other's): per stage,
+//     cp.async.bulk of the item's weight and scale
 //     blocks (contiguous per row tile in the fragment-major layout) and of the
 //     pass's activation rows (hidden rows in phase A, intermediate rows in
 //     phase B) into a shared-memory ring; completion via mbarrier tx-count.
 //     Phase-B activation copies wait (bounded) until every phase-A item pass
 //     of the same expert has published its intermediate rows; the weight
-//     copies of that stage are issued before the wait.  The producer shares
-//     its SM sub-partition with busy consumer warps, so stages are large
+//     copies of that stage are issued before the wait.  The producers share
+//     their SM sub-partitions with busy consumer warps, so stages are large
 //     (few per-stage instruction chains).
 //   * 16 consumer warps: a warp covers Rw row tiles of the item for its share
 //     of the stage's k-chunks, so each activation fragment (ldmatrix) feeds Rw
